@@ -1,0 +1,372 @@
+"""Benchmark of the fused all-gather GEMM (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mlp70b|qkv8b|smoke]
+
+Launched as one process per GPU (torchrun for N > 1).  A "step" is one launch
+of C_r = AllGather(A_r) . B_r^T over the workload's shapes on every rank:
+
+  mlp70b (default)  Llama-3-70B MLP gate+up projection: M = 16384 tokens
+                    (M/N per rank), K = 8192, 57344 output columns in total
+                    (57344/N per rank), bf16, fp32 accumulate, bf16 output;
+  qkv8b             Llama-3-8B QKV projection: M = 8192, K = 4096, N = 6144;
+  smoke             M = 1024, K = 1024, N = 1024.
+
+Inputs are synthetic, seeded per rank on the device: activations ~ N(0, 1),
+weights ~ N(0, 0.02).  They are larger than L2 at mlp70b/qkv8b, so no flush
+is inserted between timed steps (smoke flushes L2 with a 256 MiB write).
+
+value   whole-job TFLOP/s = 2*M*K*N_total / (max over ranks of the device time
+        per step), inputs resident in HBM;
+e2e     the same through the public API with host buffers: each step copies
+        A_r from pinned host memory to the GPU, launches, and copies C_r back;
+unfused the baseline of an NCCL all-gather followed by a cuBLAS GEMM (torch);
+cpu_baseline  the CPU oracle's fp32 GEMM on a bounded sample (rank 0, N = 1).
+
+--impl reference times the reference's CPU path for this workload: the
+reference has no CPU GEMM of its own, so this is the oracle's restatement of
+its fp32 check (include/reference_matmul.cuh:17-32), multithreaded, on a
+bounded sample per step; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "mlp70b": dict(name="llama3-70b-mlp-gate-up", M=16384, K=8192, N=57344),
+    "qkv8b": dict(name="llama3-8b-qkv", M=8192, K=4096, N=6144),
+    "smoke": dict(name="smoke-1024", M=1024, K=1024, N=1024),
+}
+NVLINK_GBS = 770.0        # measured peer copy per direction on this pool
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return dict(bf16=float(d["bf16_tflops"]), bf16_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                    hbm=float(d["hbm_gbs"]), source="measured")
+    except Exception:
+        return dict(bf16=FALLBACK_BF16_TFLOPS, bf16_sustained=1400.0, hbm=FALLBACK_HBM_GBS, source="fallback")
+
+
+def ncu_traffic(workload):
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"ag_gemm_kernel_{workload}.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        mhz = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        max_mhz = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max_mhz, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import numpy as np
+
+    import __graft_entry__ as ge
+
+    oracle = ge.load_oracle()
+    w = WORKLOADS[args.workload]
+    world = args.gpus
+    K = w["K"]
+    n_r = w["N"] // world
+    rows, cols = 256, min(2048, n_r)
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((rows, K), dtype=np.float32)
+    B = (rng.standard_normal((cols, K), dtype=np.float32) * 0.02).astype(np.float32)
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.gemm_f32(A, B, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.gemm_f32(A, B, threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    tflops = 2.0 * rows * cols * K / dt / 1e12
+    sample = f"{rows} rows x {cols} cols x K={K} of the {w['name']} GEMM per step (fp32, {threads} threads)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_of(args.workload, world),
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "all-gather GEMM TFLOP/s per GPU at 1/2/4/8 B200; % of roofline; vs NCCL+cuBLAS"
+
+
+def config_of(workload, world):
+    w = WORKLOADS[workload]
+    return {"workload": w["name"], "M": w["M"], "K": w["K"], "N_total": w["N"], "N_per_rank": w["N"] // world,
+            "M_per_rank": w["M"] // world, "P": world,
+            "l2": "inputs larger than L2, no flush" if workload != "smoke" else "256 MiB L2 flush between steps",
+            "parallelism": f"ag-tp{world}"}
+
+
+# ------------------------------------------------------------------ our arm
+def cpu_baseline(workload):
+    import numpy as np
+
+    import __graft_entry__ as ge
+
+    oracle = ge.load_oracle()
+    w = WORKLOADS[workload]
+    K = w["K"]
+    rows, cols = 512, 2048
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((rows, K), dtype=np.float32)
+    B = rng.standard_normal((cols, K), dtype=np.float32)
+    threads = os.cpu_count() or 1
+    oracle.gemm_f32(A[:64], B[:256], threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.gemm_f32(A, B, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > 10.0 or reps >= 50:
+            break
+    tflops = 2.0 * rows * cols * K * reps / el / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x ({rows} x {cols} x K={K}) slices of the {w['name']} GEMM, fp32, {el:.1f} s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="mlp70b", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-unfused", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        args.gpus = world
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as ge
+
+    pkg = ge.load_package()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    host_group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+
+    w = WORKLOADS[args.workload]
+    M, K, Ntot = w["M"], w["K"], w["N"]
+    m_local, n_r = M // world, Ntot // world
+    g = torch.Generator(device=dev).manual_seed(1000 * rank + 7)
+    A_r = torch.randn(m_local, K, device=dev, generator=g).bfloat16()
+    B_r = (torch.randn(n_r, K, device=dev, generator=g) * 0.02).bfloat16()
+    C_r = torch.empty(M, n_r, device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if args.workload == "smoke" else None
+
+    op = pkg.AllGatherGemm(m_local, K, host_group=host_group) if world > 1 else pkg.AllGatherGemm(m_local, K)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=host_group)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=host_group)
+        return float(t.item())
+
+    def timed(step_fn, steps):
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step_fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    def step_ours():
+        if flush is not None:
+            flush.fill_(1)
+        op(A_r, B_r, out=C_r)
+
+    for _ in range(args.warmup):
+        step_ours()
+    torch.cuda.synchronize()
+    op.check_status()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms = timed(step_ours, args.steps)
+    clk = clocks.stop()
+    op.check_status()
+    # kernel-only time of the same launches (the flush is excluded for smoke)
+    kernel_ms = ms if flush is None else timed(lambda: op(A_r, B_r, out=C_r), args.steps)
+
+    flops_step = 2.0 * M * K * Ntot
+    value = flops_step / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    flops_rank = 2.0 * M * K * n_r
+    achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
+    t_tc = flops_rank / (peaks["bf16"] * 1e12)
+    nvl_bytes = (world - 1) / world * M * K * 2 if world > 1 else 0.0
+    t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
+    t_roof = max(t_tc, t_nvl)
+    traffic = ncu_traffic(args.workload)
+    roofline = {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "achieved": achieved, "peak": peaks["bf16"],
+                "unit": "TFLOP/s", "frac": t_roof / (kernel_ms * 1e-3),
+                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
+                "traffic": traffic, "t_roof_ms": t_roof * 1e3, "t_tensor_ms": t_tc * 1e3, "t_nvlink_ms": t_nvl * 1e3,
+                "nvlink_bytes_per_rank": nvl_bytes}
+
+    out = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (A~N(0,1), B~N(0,0.02), seeded per rank)",
+           "config": config_of(args.workload, world), "tflops_per_gpu": value / world,
+           "gpu_launches": args.steps, "roofline": roofline, "clocks": clk}
+
+    # ---- unfused baseline: NCCL all-gather + cuBLAS GEMM
+    if not args.no_unfused:
+        A_full = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+        C_u = torch.empty(M, n_r, device=dev, dtype=torch.bfloat16)
+
+        def step_unfused():
+            if flush is not None:
+                flush.fill_(1)
+            if world > 1:
+                dist.all_gather_into_tensor(A_full, A_r)
+                torch.matmul(A_full, B_r.t(), out=C_u)
+            else:
+                torch.matmul(A_r, B_r.t(), out=C_u)
+
+        for _ in range(args.warmup):
+            step_unfused()
+        ums = timed(step_unfused, args.steps)
+        out["unfused_nccl_cublas"] = {"value": flops_step / (ums * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                      "ms_per_step": ums, "speedup_fused": ums / ms}
+        del A_full, C_u
+
+    # ---- end to end through the public API with host buffers
+    if not args.no_e2e:
+        A_host = torch.empty(m_local, K, dtype=torch.bfloat16, pin_memory=True)
+        A_host.copy_(A_r)
+        C_host = torch.empty(M, n_r, dtype=torch.bfloat16, pin_memory=True)
+        A_dev = torch.empty_like(A_r)
+
+        def step_e2e():
+            A_dev.copy_(A_host, non_blocking=True)
+            op(A_dev, B_r, out=C_r)
+            C_host.copy_(C_r, non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            step_e2e()
+        e2e_steps = max(2, min(args.steps, 5))
+        ems = timed(step_e2e, e2e_steps)
+        out["e2e"] = {"value": flops_step / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": A_host.numel() * 2, "d2h_bytes_per_step": C_host.numel() * 2,
+                      "ms_per_step": ems, "steps": e2e_steps}
+        out["gpu_launches"] = args.steps + e2e_steps
+        op.check_status()
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.workload)
+
+    op.close()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

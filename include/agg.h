@@ -1,0 +1,217 @@
+/*
+ * agg.h — C ABI of the B200 (sm_100a) fused all-gather GEMM library, libagg.so.
+ *
+ * The library computes, on each of P ranks (one GPU each),
+ *     C_r[M, N_r] = AllGather_r(A_r)[M, K] . B_r[N_r, K]^T
+ * bf16 (or e4m3) inputs, fp32 accumulation in tensor memory, bf16 output,
+ * in ONE kernel: producer warps broadcast this rank's A shard into an NVLink
+ * multicast object with multimem.st and raise per-chunk arrival flags, while
+ * the tensor-core warps already consume the arrived tiles.
+ *
+ * Every entry point takes plain pointers and sizes; CUDA streams are passed as
+ * `void*` (a cudaStream_t, NULL = legacy default stream).  Return values are
+ * 0 on success and a negative AGG_E* code otherwise; agg_last_error() gives
+ * the message of the calling thread's last failure.
+ *
+ * Interfaces of the reference (ShawnWeiChew/vmm-experiment) replaced here:
+ *   agg_spmm_init / agg_rank_info   minfer_spmm_init + RankState
+ *                                   (vmm/multimem.cu:74-101, include/multimem.cuh:11-23)
+ *   agg_vm_alloc / agg_vm_map /     vm_alloc / vm_map (include/vmm.cuh:12-38); the
+ *   agg_vm_set_access               access grant the reference leaves out is added
+ *   agg_args / agg_launch           fused_globals<128,256,2> +
+ *                                   launch_ag_gemm_warp_specialized<128,256,2,5>
+ *                                   (call site vmm/main.cpp:226,272-296; the kernel's
+ *                                   own source is an absent submodule)
+ *   agg_multimem_ops_test           multicast_ops_kernel (include/test_kernel.cuh:46-74)
+ *   agg_alias_fence                 multicast_alias_fence_kernel (include/test_kernel.cuh:41-44)
+ *   agg_mm_barrier                  mm_barrier (vmm/multimem.cu:103-119), bounded
+ *   agg_mc_broadcast / agg_verify_* multicast push + byte-exact verify
+ *                                   (vmm/test_vmm_multicast_speed.cu:99-126,172-194)
+ *   agg_mp_*                        no counterpart (the reference is one process with a
+ *                                   thread per GPU); POSIX-fd export/import of the same
+ *                                   handles so ranks can be separate processes.
+ */
+#ifndef AGG_H_
+#define AGG_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- error codes ---------------------------------------------------------------- */
+#define AGG_OK 0
+#define AGG_EINVAL (-1)        /* bad argument (shape, alignment, rank/device mismatch) */
+#define AGG_ECUDA (-2)         /* a CUDA runtime call failed */
+#define AGG_EDRIVER (-3)       /* a CUDA driver call failed */
+#define AGG_ENOMULTICAST (-4)  /* a device lacks NVLink multicast support */
+#define AGG_ESTATE (-5)        /* called in the wrong order / not initialised */
+#define AGG_ESYS (-6)          /* an OS call (socket, fd passing) failed */
+#define AGG_ETIMEOUT (-7)      /* a device-side wait ran out (see agg_status_* below) */
+
+/* ---- device status word (written by kernels, read by the host) ------------------- */
+/* 0 = ok.  Otherwise bits 0-7 hold the failing role, bits 8-31 where it gave up.    */
+#define AGG_STATUS_OK 0u
+#define AGG_ROLE_TMA 1u        /* operand loader waiting for a free stage            */
+#define AGG_ROLE_MMA 2u        /* tensor-core issuer waiting for operands/TMEM        */
+#define AGG_ROLE_EPI 3u        /* epilogue waiting for an accumulator                 */
+#define AGG_ROLE_FLAG 4u       /* loader waiting for a remote chunk's arrival flag    */
+#define AGG_ROLE_PROD 5u       /* multicast producer waiting for the previous launch  */
+#define AGG_ROLE_BARRIER 6u    /* mm_barrier gave up                                  */
+#define AGG_ROLE_DRAIN 7u      /* teardown wait for in-flight copies / MMAs          */
+
+/* ---- dtypes ----------------------------------------------------------------------- */
+#define AGG_DTYPE_BF16 0
+#define AGG_DTYPE_E4M3 1
+
+/* ---- slab / flag layout constants ------------------------------------------------ */
+#define AGG_MAX_RANKS 8
+#define AGG_TILE_M 128                 /* rows per arrival chunk (= MMA tile height)     */
+#define AGG_MAX_CHUNKS 1024            /* per source rank: M/P <= 131072 rows            */
+#define AGG_PARTS_PER_CHUNK 64         /* arrivals per chunk per launch (flag target =   */
+                                       /* epoch * AGG_PARTS_PER_CHUNK)                   */
+#define AGG_FLAG_BYTES (64u << 10)     /* flag area zeroed at init                       */
+#define AGG_FLAG_CHUNK_OFF 0u          /* u32 [AGG_MAX_RANKS][AGG_MAX_CHUNKS] arrivals   */
+#define AGG_FLAG_DONE_OFF (32u << 10)  /* u32 end-of-launch counter                      */
+#define AGG_FLAG_USER_OFF (36u << 10)  /* free for mm_barrier rows / tests (28 KiB)      */
+
+/* Per-rank view of the multicast slab (RankState of the reference, C layout). */
+typedef struct agg_rank_info {
+    uint64_t uc;                        /* this GPU's physical slab, unicast VA          */
+    uint64_t mc;                        /* the multicast VA of the same slab             */
+    uint64_t peer_uc[AGG_MAX_RANKS];    /* every rank's slab as mapped in this process  */
+    uint64_t slab_bytes;                /* size of each slab                              */
+    uint64_t flag_off;                  /* offset of the flag area inside the slab       */
+    int32_t rank, world, device;
+    int32_t reserved;
+} agg_rank_info;
+
+/*
+ * Launch arguments: the fields of the reference's fused_globals in its order
+ * (A, A_local_buf, B, C, A_copy_ready, A_copy_epoch, dev_idx, M, N;
+ * vmm/main.cpp:272-294) followed by what the reference fixed at compile time.
+ */
+typedef struct agg_args {
+    /* A: the distributed activation.  A_mc is the multicast VA where gathered A
+       starts (rank s's shard at A_mc + s*M_local*K*elem); A_peer[s] are the
+       unicast VAs of every rank's slab (informational; the kernel only reads
+       its own GPU's memory). */
+    uint64_t A_mc;
+    uint64_t A_peer[AGG_MAX_RANKS];
+    /* Gathered A [M, K] on this GPU (unicast VA of the same slab region). */
+    void* A_local_buf;
+    /* B_r [N_r, K] row-major (K-major), this rank's weight shard. */
+    const void* B;
+    /* C_r [M, N_r] row-major bf16 output. */
+    void* C;
+    /* Arrival flags, this GPU's unicast view (u32 [AGG_MAX_RANKS][AGG_MAX_CHUNKS]). */
+    uint32_t* A_copy_ready;
+    /* Launch epoch, >= 1, incremented by exactly one per launch on every rank. */
+    uint32_t A_copy_epoch;
+    int32_t dev_idx; /* this rank */
+    int32_t M;       /* total rows of gathered A = world * M_local */
+    int32_t N;       /* N_r, columns of this rank's output */
+    /* ---- added: what the reference template fixed at compile time ---- */
+    int32_t K;
+    int32_t world;
+    int32_t dtype;                 /* AGG_DTYPE_BF16 / AGG_DTYPE_E4M3 */
+    int32_t flags;                 /* reserved, 0 */
+    const void* A_src;             /* this rank's shard [M/world, K]; NULL = inside A_local_buf */
+    uint32_t* A_copy_ready_mc;     /* multicast view of the flag array */
+    uint32_t* done_uc;             /* end-of-launch counter, unicast view */
+    uint32_t* done_mc;             /* end-of-launch counter, multicast view */
+    const float* scale_a;          /* e4m3: per-row scale of gathered A [M] */
+    const float* scale_b;          /* e4m3: per-row scale of B_r [N_r] (per output column) */
+    uint32_t* status;              /* device status word (AGG_STATUS_*), may be NULL */
+    uint64_t timeout_ns;           /* bound on every device-side wait; 0 = 10 s */
+} agg_args;
+
+/* ---- library ---------------------------------------------------------------------- */
+int agg_version(void);                 /* 100 * major + minor */
+int agg_abi_sizes(size_t* args_bytes, size_t* rank_info_bytes); /* sizeof(agg_args/agg_rank_info) */
+const char* agg_last_error(void);      /* message of this thread's last failure */
+int agg_device_count(void);
+
+/* ---- VMM helpers (include/vmm.cuh:12-38) ------------------------------------------- */
+int agg_vm_alloc(uint64_t* handle, size_t* allocated_size, size_t size, int device_id);
+int agg_vm_map(uint64_t* ptr, uint64_t handle, size_t size);
+int agg_vm_set_access(uint64_t ptr, size_t size, const int* devices, int ndevices);
+int agg_vm_unmap_free(uint64_t ptr, size_t size);
+int agg_vm_release(uint64_t handle);
+
+/* ---- one process, one thread per GPU (minfer_spmm_init, vmm/multimem.cu:74-101) --- */
+/* rank must equal device; the first caller creates the multicast object for
+   devices 0..world-1; every rank binds its own slab.  Idempotent per rank. */
+int agg_spmm_init(int rank, int world, int device, size_t data_bytes, agg_rank_info* out);
+/* Unmaps and releases this rank's slab; the multicast object goes with the last rank. */
+int agg_spmm_finalize(int rank);
+
+/* ---- one process per GPU: POSIX-fd handle exchange over abstract unix sockets ----- */
+/* Call order on every rank, with a host barrier between the steps:
+     agg_mp_open -> barrier -> agg_mp_exchange -> agg_mp_add_device -> barrier ->
+     agg_mp_bind -> barrier -> (launches) -> agg_mp_close.
+   job_id must be the same string on every rank and unique on the machine. */
+typedef struct agg_mp_ctx agg_mp_ctx;
+int agg_mp_open(int rank, int world, int device, size_t data_bytes, const char* job_id,
+                agg_mp_ctx** out);
+int agg_mp_exchange(agg_mp_ctx* ctx);
+int agg_mp_add_device(agg_mp_ctx* ctx);
+int agg_mp_bind(agg_mp_ctx* ctx, agg_rank_info* out);
+int agg_mp_close(agg_mp_ctx* ctx);
+
+/* ---- the fused all-gather GEMM ----------------------------------------------------- */
+/* Enqueue one launch on `stream`.  Shapes: M % world == 0, (M/world) % 128 == 0
+   when world > 1, K % 8 == 0, N % 8 == 0 (16-byte row pitch).  Returns AGG_EINVAL
+   without launching on bad arguments. */
+int agg_launch(const agg_args* args, void* stream);
+/* Single-GPU GEMM through the same kernel: C[M,N] = A[M,K] . B[N,K]^T (bf16). */
+int agg_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, uint32_t* status,
+                  void* stream);
+/* Same for e4m3 operands with per-row scales of A [M] and of B [N], bf16 output. */
+int agg_gemm_e4m3(const void* A, const void* B, void* C, const float* scale_a,
+                  const float* scale_b, int M, int N, int K, uint32_t* status, void* stream);
+/* Number of SMs the persistent grid uses on the current device (0 on failure). */
+int agg_num_sms(void);
+
+/* ---- multicast primitives ---------------------------------------------------------- */
+/* Broadcast `bytes` (multiple of 16) from local `src` to `mc_dst` with 16-byte
+   multimem.st, then raise the u32 at `flag_mc` by one (release, system scope)
+   when flag_mc is not NULL. */
+int agg_mc_broadcast(const void* src, uint64_t mc_dst, size_t bytes, uint32_t* flag_mc,
+                     int num_blocks, void* stream);
+/* Count 64-bit words of `data` (bytes/8 of them) that differ from `expect`
+   into *mismatches (device u64, accumulated). */
+int agg_verify_bytes(const void* data, const void* expect, size_t bytes,
+                     unsigned long long* mismatches, void* stream);
+/* Count words of a gathered buffer [world][shard_bytes] whose bytes are not
+   (source rank + 1) repeated (vmm/test_vmm_multicast_speed.cu:99-114). */
+int agg_verify_pattern_gather(const void* gathered, size_t shard_bytes, int world,
+                              unsigned long long* mismatches, void* stream);
+/* fence.proxy.alias on the stream (include/test_kernel.cuh:41-44). */
+int agg_alias_fence(void* stream);
+/* The reference's multimem smoke (include/test_kernel.cuh:46-74) on a 16-byte
+   record {reduce_input, store_output, red_target, reduced_local} at mc_rec:
+   ld_reduce.add.f32 of reduce_input over all GPUs, st of the sum to
+   store_output, red.add.f32 of `addend` to red_target, sum also to *reduced_out. */
+int agg_multimem_ops_test(uint64_t mc_rec, float* reduced_out, float addend, void* stream);
+/* Vectorised variants: v4 ld_reduce.add.f32 over n4 float4s (sum of all GPUs' copies
+   written to local out), and v4 red.add.f32 of `addend` into every GPU's copy. */
+int agg_multimem_ld_reduce_v4(uint64_t mc_src, float* out, size_t n4, void* stream);
+int agg_multimem_red_add_v4(uint64_t mc_dst, float addend, size_t n4, void* stream);
+/* mm_barrier (vmm/multimem.cu:103-119) as a kernel of `blocks` CTAs: each CTA adds 1
+   to mc_flags[row*256 + cta] and waits (bounded by timeout_ns) until its unicast
+   copy reaches `target`; a timeout is recorded in *status (AGG_ROLE_BARRIER). */
+int agg_mm_barrier(uint32_t* mc_flags, const uint32_t* uc_flags, int row, uint32_t target,
+                   int blocks, uint32_t* status, uint64_t timeout_ns, void* stream);
+/* Device-side bounded wait on a u32 flag reaching `target` (no writer needed):
+   the failure-detection path; records AGG_ROLE_FLAG on timeout. */
+int agg_wait_flag(const uint32_t* flag, uint32_t target, uint32_t* status, uint64_t timeout_ns,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AGG_H_ */

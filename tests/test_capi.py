@@ -1,0 +1,79 @@
+"""The C-ABI library loads on a host without a GPU and exports what include/agg.h declares."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "agg.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(agg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol(pkg):
+    L = pkg.lib()
+    declared = header_functions()
+    assert len(declared) >= 25
+    nm = subprocess.run(["nm", "-D", "--defined-only", pkg.agg.LIB_PATH], capture_output=True, text=True,
+                        check=True).stdout
+    exported = set(re.findall(r" T (agg_[a-z0-9_]+)", nm))
+    missing = [f for f in declared if f not in exported]
+    assert not missing, f"declared in agg.h but not exported: {missing}"
+    assert set(pkg.agg.EXPORTS) == set(declared)
+    for f in declared:
+        getattr(L, f)
+
+
+def test_library_has_no_driver_link_dependency(pkg):
+    ldd = subprocess.run(["ldd", pkg.agg.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in ldd and "libtorch" not in ldd
+
+
+def test_abi_struct_sizes_match_python(pkg):
+    a = ctypes.c_size_t()
+    r = ctypes.c_size_t()
+    assert pkg.lib().agg_abi_sizes(ctypes.byref(a), ctypes.byref(r)) == 0
+    assert a.value == ctypes.sizeof(pkg.agg.agg_args) == 200
+    assert r.value == ctypes.sizeof(pkg.agg.agg_rank_info)
+    assert pkg.lib().agg_version() == 100
+
+
+def test_launch_rejects_bad_arguments_before_touching_the_gpu(pkg):
+    agg = pkg.agg
+    L = pkg.lib()
+    base = dict(M=256, N=256, K=256, world=1, dev_idx=0, A_copy_epoch=1)
+
+    def launch(**kw):
+        a = agg.agg_args()
+        a.A_src, a.B, a.C = 0x1000, 0x2000, 0x3000
+        for k, v in {**base, **kw}.items():
+            setattr(a, k, v)
+        return L.agg_launch(ctypes.byref(a), None)
+
+    assert launch(N=12) == -1                 # N*2 bytes not a 16-byte pitch
+    assert launch(K=12) == -1                 # K*2 bytes not a 16-byte pitch
+    assert launch(world=9) == -1
+    assert launch(world=2, M=256 + 2) == -1   # M not divisible by world
+    assert launch(world=2, M=2 * 100) == -1   # shard not a multiple of 128 rows
+    assert launch(world=2, M=512) == -1       # multicast buffers missing
+    assert launch(dtype=7) == -1
+    assert launch(dtype=1) == -1              # e4m3 without scales
+    assert b"scale" in L.agg_last_error()
+
+
+def test_errors_without_gpu_are_reported_not_raised(pkg):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    L = pkg.lib()
+    assert L.agg_device_count() == 0
+    info = pkg.agg.agg_rank_info()
+    rc = L.agg_spmm_init(0, 2, 0, 1 << 20, ctypes.byref(info))
+    assert rc < 0 and L.agg_last_error()
+    assert L.agg_spmm_init(0, 2, 1, 1 << 20, ctypes.byref(info)) == -1  # rank != device

@@ -1,0 +1,147 @@
+"""Parity of the sm_100a kernel at world = 1 (a plain GEMM through agg_launch)
+against the CPU oracle, the reference's own cuBLAS check and torch.
+
+Tolerance (bf16 inputs, fp32 accumulate, bf16 output): the reference's
+check_close (atol 0.1, rtol 0.02, include/reference_matmul.cuh:103-104) on
+every element, and a normwise max|C - C_ref| / max|C_ref| <= 1e-2.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-2
+
+
+def to_dev_bf16(bits, shape):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16).reshape(shape)).view(torch.bfloat16).cuda()
+
+
+def run_gemm(pkg, A, B):
+    import torch
+
+    status = torch.zeros(1, dtype=torch.int32, device=A.device)
+    C = pkg.gemm(A, B, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, pkg.agg.describe_status(int(status.item()))
+    return C
+
+
+def check_against(oracle, got, want):
+    stats = oracle.error_stats(got, want)
+    bad, where = oracle.check_close(got, want)
+    assert stats["nan"] == 0
+    assert bad == 0, f"{bad} elements outside check_close, first at {where}; {stats}"
+    assert stats["max_rel_err"] <= MAX_REL, stats
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (128, 256, 64),      # one tile, one k-block
+    (256, 512, 1024),    # smoke-sized
+    (1024, 512, 1024),   # the smoke workload's gathered shape per rank
+    (200, 264, 136),     # ragged M, N, K (zero-filled tails, clipped stores)
+    (1, 8, 8),           # minimum shape
+    (77, 1000, 40),      # K shorter than one k-block
+    (640, 768, 4096),    # several waves of k-blocks, N not a multiple of 256
+])
+def test_gemm_matches_oracle(pkg, oracle, gpu, M, N, K):
+    a_bits, a_ref = oracle.fill_random_bf16(1, M * K)
+    b_bits, b_ref = oracle.fill_random_bf16(2, N * K)
+    C = run_gemm(pkg, to_dev_bf16(a_bits, (M, K)), to_dev_bf16(b_bits, (N, K)))
+    want = oracle.gemm_f64(a_ref.reshape(M, K), b_ref.reshape(N, K)).astype(np.float32)
+    check_against(oracle, C.float().cpu().numpy(), want)
+
+
+def test_gemm_matches_reference_cublas_path(pkg, oracle, gpu):
+    """The reference's own reference_matmul_cublas + check_close (oracle/_ref)."""
+    R = oracle.ref_lib()
+    if R is None:
+        pytest.skip("oracle/_ref/libref.so not built")
+    M, N, K = 1024, 512, 1024
+    A_bits, A_ref, B_bits, B_ref = oracle.harness_inputs(2, M // 2, K, N)
+    a_bits = np.concatenate(A_bits)
+    a_ref = np.concatenate(A_ref)
+    C = run_gemm(pkg, to_dev_bf16(a_bits, (M, K)), to_dev_bf16(B_bits[1], (N, K)))
+    got = np.ascontiguousarray(C.float().cpu().numpy())
+    want = np.empty((M, N), np.float32)
+    f32p = ctypes.POINTER(ctypes.c_float)
+    assert R.ref_matmul_cublas(a_ref.ctypes.data_as(f32p), M, K, B_ref[1].ctypes.data_as(f32p), N,
+                               want.ctypes.data_as(f32p)) == 0
+    assert R.ref_check_close(got.ctypes.data_as(f32p), want.ctypes.data_as(f32p), M, N, 0.1, 0.02) == 1
+    check_against(oracle, got, want)
+
+
+def test_gemm_matches_torch_fp32(pkg, gpu):
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    M, N, K = 2048, 3072, 4096
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+    C = run_gemm(pkg, A, B)
+    ref = A.float() @ B.float().t()
+    err = (C.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err <= MAX_REL, err
+
+
+def test_repeated_launches_are_identical(pkg, gpu):
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn(512, 1024, device="cuda", generator=g).bfloat16()
+    B = torch.randn(768, 1024, device="cuda", generator=g).bfloat16()
+    C0 = run_gemm(pkg, A, B)
+    for _ in range(3):
+        assert torch.equal(run_gemm(pkg, A, B), C0)
+
+
+def sampled_check(pkg, oracle, M, N, K, seed):
+    """Full-size shape: every output element is computed, a random sample is
+    checked against fp64 dot products of the same bf16 inputs."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+    C = run_gemm(pkg, A, B)
+    rows = torch.randint(0, M, (512,), generator=g, device="cuda")
+    cols = torch.randint(0, N, (512,), generator=g, device="cuda")
+    a = A[rows].double()
+    b = B[cols].double()
+    want = (a * b).sum(dim=1)
+    got = C[rows, cols].double()
+    scale = want.abs().max().item()
+    assert (got - want).abs().max().item() <= MAX_REL * scale
+    # and every element of C was written with a finite value
+    assert torch.isfinite(C).all().item()
+
+
+def test_gemm_llama8b_qkv_shape_sampled(pkg, oracle, gpu):
+    sampled_check(pkg, oracle, 8192, 6144, 4096, 11)
+
+
+def test_gemm_llama70b_mlp_shape_sampled(pkg, oracle, gpu):
+    # one rank's share at P=8 (N_r = 57344 / 8)
+    sampled_check(pkg, oracle, 16384, 7168, 8192, 12)
+
+
+def test_timeout_status_reported(pkg, gpu):
+    """A device wait that nothing satisfies ends with a status word, not a hang."""
+    import torch
+
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L = pkg.lib()
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.agg_wait_flag(ctypes.c_void_p(flag.data_ptr()), 1, ctypes.c_void_p(status.data_ptr()),
+                           200_000_000, s) == 0
+    torch.cuda.synchronize()
+    word = int(status.item())
+    assert word & 0xFF == 4  # AGG_ROLE_FLAG
+    # the context is still usable
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum().item()) == 8.0

@@ -1,0 +1,686 @@
+// The fused all-gather GEMM for sm_100a.
+//
+//   C_r[M, N_r] = AllGather(A_r)[M, K] . B_r[N_r, K]^T
+//
+// One persistent, warp-specialised kernel per rank (one CTA per SM, 256 threads):
+//
+//   warp 0      operand loader: one lane issues TMA loads of A (128 x 128 B) and
+//               B (256 x 128 B) k-blocks into a 4-stage shared-memory ring.  A tile
+//               of a remote rank's rows is loaded only after that chunk's arrival
+//               flag (in this GPU's own slab) has reached its target.
+//   warp 1      tensor-core issuer: owns 512 TMEM columns (two 128 x 256 fp32
+//               accumulators), one lane issues tcgen05.mma (M=128, N=256, K=16
+//               for bf16 / K=32 for e4m3) and tcgen05.commit to free stages and
+//               publish finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld 32 TMEM lanes x 64 columns at a time, (e4m3:
+//               apply per-row x per-column scales), round to bf16, stage through a
+//               128 B-swizzled buffer and TMA-store 32 x 64 boxes of C.  Runs one
+//               accumulator behind the MMAs (double buffering).
+//   warps 6-7   multicast producers (world > 1): stream this rank's A shard from
+//               HBM and write it with 16-byte multimem.st into the NVLink multicast
+//               object, so NVSwitch delivers it into every GPU's slab; after each
+//               part a release-ordered multimem.red raises that chunk's flag on
+//               every GPU.
+//
+// Tile order: this rank's own rows first (no wait), then the remote chunks in
+// the order they are produced (chunk-major, sources r+1, r+2, ...), grouped
+// `group_m` m-tiles at a time so concurrently running CTAs share A and B in L2.
+//
+// Every wait is bounded by the launch's deadline; a timeout writes the status
+// word and all roles wind down (no traps, no unbounded spins), TMEM is always
+// released.
+//
+// Reference: the kernel replaces launch_ag_gemm_warp_specialized<128,256,2,5>
+// called at vmm/main.cpp:296 with the fused_globals of vmm/main.cpp:272-294
+// (its own source is in an absent submodule).  The numerics follow the
+// reference's check, include/reference_matmul.cuh:17-32 / 59-77: bf16 inputs,
+// fp32 accumulation.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "agg.h"
+#include "agg_internal.h"
+#include "agg_ptx.cuh"
+
+namespace agg {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK_BYTES = 128;  // one 128-byte swizzle row: 64 bf16 or 128 e4m3
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK_BYTES;  // 16 KiB
+constexpr int B_STAGE_BYTES = BN * BK_BYTES;  // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int EPI_WARPS = 4;
+constexpr int EPI_ROWS = 32;
+constexpr int EPI_COLS = 64;
+constexpr int EPI_BUF_BYTES = EPI_ROWS * EPI_COLS * 2;  // 4 KiB of bf16
+constexpr int PROD_WARPS = 2;
+constexpr int NUM_WARPS = 2 + EPI_WARPS + PROD_WARPS;
+constexpr int NUM_THREADS = NUM_WARPS * 32;
+constexpr uint32_t TMEM_COLS = 512;
+
+constexpr int SMEM_STAGE_OFF = 0;
+constexpr int SMEM_EPI_OFF = STAGES * STAGE_BYTES;
+constexpr int SMEM_BAR_OFF = SMEM_EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES;
+constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+constexpr int SMEM_TMEM_SLOT_OFF = SMEM_BAR_OFF + NUM_BARS * 8;
+constexpr int SMEM_USED = SMEM_TMEM_SLOT_OFF + 16;
+constexpr int SMEM_ALLOC = SMEM_USED + 1024;  // slack to align the base to 1024 B
+static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+static_assert(SMEM_EPI_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "swizzle alignment");
+
+constexpr uint32_t IDESC_BF16 = make_idesc(1, 1, BM, BN);
+constexpr uint32_t IDESC_E4M3 = make_idesc(0, 0, BM, BN);
+
+struct alignas(64) KParams {
+    CUtensorMap tm_a_src;   // this rank's shard (the whole A when world == 1)
+    CUtensorMap tm_a_gath;  // gathered A [M, K] in this GPU's slab
+    CUtensorMap tm_b;       // B_r [N, K]
+    CUtensorMap tm_c;       // C_r [M, N] bf16
+    const uint4* a_src;     // shard, for the producers' loads
+    uint4* a_mc;            // multicast VA of this rank's slot in gathered A
+    unsigned long long shard_bytes;
+    unsigned long long chunk_bytes;
+    unsigned long long part_bytes;
+    uint32_t* flags_uc;
+    uint32_t* flags_mc;
+    uint32_t* done_uc;
+    uint32_t* done_mc;
+    uint32_t* cta_counter;
+    const float* scale_a;
+    const float* scale_b;
+    uint32_t* status;
+    unsigned long long timeout_ns;
+    uint32_t epoch;
+    int rank, world;
+    int M, N, K;
+    int m_local;
+    int num_m_tiles, num_n_tiles, num_tiles, num_kb;
+    int ppc, num_parts;
+    int group_m;
+    int dtype;
+};
+
+// Position `pos` of the m-tile visiting order -> global m-tile index.
+__device__ __forceinline__ int m_tile_at(const KParams& p, int pos) {
+    if (p.world == 1) return pos;
+    const int L = p.m_local / BM;
+    if (pos < L) return p.rank * L + pos;
+    const int q = pos - L;
+    const int c = q / (p.world - 1);
+    const int k = q - c * (p.world - 1);
+    int s = p.rank + 1 + k;
+    if (s >= p.world) s -= p.world;
+    return s * L + c;
+}
+
+__device__ __forceinline__ void tile_coords(const KParams& p, int t, int& mt, int& nt) {
+    const int per_group = p.group_m * p.num_n_tiles;
+    const int g = t / per_group;
+    const int j = t - g * per_group;
+    const int first = g * p.group_m;
+    const int gs = min(p.group_m, p.num_m_tiles - first);
+    nt = j / gs;
+    mt = m_tile_at(p, first + (j - nt * gs));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// ---------------------------------------------------------------- roles
+__device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uint64_t* full,
+                                            uint64_t* empty, const Deadline& dl) {
+    tma_prefetch_desc(&p.tm_a_src);
+    tma_prefetch_desc(&p.tm_b);
+    if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
+    const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
+    const int L = p.m_local / BM;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used = 0, last_par = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        const CUtensorMap* tma = &p.tm_a_src;
+        int a_row;
+        if (p.world == 1) {
+            a_row = mt * BM;
+        } else {
+            const int src = mt / L;
+            if (src == p.rank) {
+                a_row = (mt - src * L) * BM;
+            } else {
+                const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (mt - src * L);
+                if (!wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl)) {
+                    record_failure(p.status, AGG_ROLE_FLAG, static_cast<uint32_t>(mt));
+                    ok = false;
+                    break;
+                }
+                // The chunk arrived through the multicast alias and is read here
+                // through the unicast alias by the async (TMA) proxy.
+                fence_proxy_alias();
+                fence_proxy_async_global();
+                tma = &p.tm_a_gath;
+                a_row = mt * BM;
+            }
+        }
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, dl)) {
+                record_failure(p.status, AGG_ROLE_TMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            uint8_t* sa = smem + SMEM_STAGE_OFF + stage * STAGE_BYTES;
+            uint8_t* sb = sa + A_STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+            tma_load_2d(tma, sa, &full[stage], kb * kb_elems, a_row);
+            tma_load_2d(&p.tm_b, sb, &full[stage], kb * kb_elems, nt * BN);
+            used |= 1u << stage;
+            last_par = (last_par & ~(1u << stage)) | (phase << stage);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+    // Never leave the CTA with TMA writes still landing in shared memory.
+    for (int s = 0; s < STAGES; ++s)
+        if (used & (1u << s))
+            if (!mbar_wait_for(&full[s], (last_par >> s) & 1u, 200000000ull))
+                record_failure(p.status, AGG_ROLE_DRAIN, 1u);
+}
+
+__device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base,
+                                         uint64_t* full, uint64_t* empty, uint64_t* tfull,
+                                         uint64_t* tempty, uint64_t* drain, const Deadline& dl) {
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    const uint32_t idesc = f8 ? IDESC_E4M3 : IDESC_BF16;
+    const int k_steps = 4;                      // 128-byte k-block / 32 bytes per MMA
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, dl)) {
+            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+            break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait(&full[stage], phase, dl)) {
+                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + SMEM_STAGE_OFF + stage * STAGE_BYTES);
+            const uint64_t adesc = sw128_kmajor_desc(sa);
+            const uint64_t bdesc = sw128_kmajor_desc(sa + A_STAGE_BYTES);
+#pragma unroll
+            for (int k = 0; k < k_steps; ++k) {
+                // +32 bytes along K inside the 128-byte swizzle row (>> 4 in the descriptor)
+                const uint64_t off = static_cast<uint64_t>(k * 2);
+                const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+                if (f8)
+                    umma_f8(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                else
+                    umma_f16(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+            }
+            umma_commit(&empty[stage]);  // stage is free once these MMAs have read it
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // accumulator complete
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+    // Every MMA this thread issued has finished once `drain` flips.
+    umma_commit(drain);
+    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+}
+
+__device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base,
+                                              uint64_t* tfull, uint64_t* tempty, int warp,
+                                              const Deadline& dl) {
+    const int eg = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t lane = lane_id();
+    uint8_t* stg = smem + SMEM_EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        int got = 1;
+        if (lane == 0) got = mbar_wait(&tfull[acc], acc_phase, dl) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, static_cast<uint32_t>(t));
+            break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + static_cast<uint32_t>(acc * BN);
+        const int row0 = mt * BM + eg * 32;
+        float row_scale = 1.0f;
+        if (f8) {
+            const int row = row0 + static_cast<int>(lane);
+            row_scale = row < p.M ? __ldg(p.scale_a + row) : 0.0f;
+        }
+#pragma unroll 1
+        for (int j = 0; j < BN / EPI_COLS; ++j) {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS), r0);
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS + 32), r1);
+            tmem_wait_ld();
+            const int col0 = nt * BN + j * EPI_COLS;
+            uint32_t packed[32];
+            if (f8) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]) * row_scale * s0,
+                                            __uint_as_float(r0[2 * i + 1]) * row_scale * s1);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 32 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]) * row_scale * s0,
+                                                 __uint_as_float(r1[2 * i + 1]) * row_scale * s1);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[16 + i] =
+                        pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+            }
+            // The buffer is free once the TMA store issued two chunks ago has read it.
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            uint8_t* b = stg + buf * EPI_BUF_BYTES;
+            const uint32_t row_base = smem_u32(b) + lane * 128u;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t addr = row_base + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+                             "r"(packed[4 * c]), "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]),
+                             "r"(packed[4 * c + 3])
+                             : "memory");
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&p.tm_c, b, col0, row0);
+                bulk_commit_group();
+            }
+            buf ^= 1;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+}
+
+__device__ __forceinline__ void role_producer(const KParams& p, int pw, const Deadline& dl) {
+    const uint32_t lane = lane_id();
+    int ok = 1;
+    if (p.epoch > 1) {
+        // Every rank must be done reading the previous launch's gathered A
+        // before this rank overwrites its slot on all GPUs.
+        if (lane == 0)
+            ok = wait_flag_geq(p.done_uc, (p.epoch - 1u) * static_cast<uint32_t>(p.world), dl) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_PROD, 0u);
+            return;
+        }
+        fence_proxy_alias();
+    }
+    const int stride = static_cast<int>(gridDim.x) * PROD_WARPS;
+    for (int q = static_cast<int>(blockIdx.x) * PROD_WARPS + pw; q < p.num_parts; q += stride) {
+        const int c = q / p.ppc;
+        const int sub = q - c * p.ppc;
+        const unsigned long long cbeg = static_cast<unsigned long long>(c) * p.chunk_bytes;
+        unsigned long long cend = cbeg + p.chunk_bytes;
+        if (cend > p.shard_bytes) cend = p.shard_bytes;
+        const unsigned long long beg = cbeg + static_cast<unsigned long long>(sub) * p.part_bytes;
+        unsigned long long end = beg + p.part_bytes;
+        if (end > cend) end = cend;
+        if (beg < end) {
+            const uint4* s = p.a_src + beg / 16;
+            uint4* d = p.a_mc + beg / 16;
+            const unsigned long long n = (end - beg) / 16;
+            for (unsigned long long i = lane; i < n; i += 32ull * 8ull) {
+                uint4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const unsigned long long j = i + 32ull * u;
+                    if (j < n) v[u] = ld_nc_v4(s + j);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const unsigned long long j = i + 32ull * u;
+                    if (j < n) mm_st_v4(d + j, v[u]);
+                }
+            }
+        }
+        // Order this warp's multicast stores before the flag, at system scope.
+        fence_acq_rel_sys();
+        __syncwarp();
+        if (lane == 0) mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
+        if (failed(p.status)) break;
+    }
+}
+
+// ---------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_constant__ KParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR_OFF);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SMEM_TMEM_SLOT_OFF);
+
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const uint32_t lane = lane_id();
+    Deadline dl;
+    dl.end_ns = globaltimer_ns() + (p.timeout_ns ? p.timeout_ns : 10000000000ull);
+    dl.status = p.status;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        fence_mbarrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+    if (warp == 0) {
+        if (lane == 0) role_loader(p, smem, full, empty, dl);
+    } else if (warp == 1) {
+        if (lane == 0) role_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        __syncwarp();
+    } else if (warp < 2 + EPI_WARPS) {
+        role_epilogue(p, smem, tmem_base, tfull, tempty, warp, dl);
+    } else if (p.world > 1) {
+        role_producer(p, warp - 2 - EPI_WARPS, dl);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+    if (p.world > 1 && threadIdx.x == 0) {
+        // This CTA has finished reading gathered A for this launch.  The last CTA
+        // on this GPU tells every GPU (release, system scope).
+        __threadfence();
+        const uint32_t prev = atomicAdd(p.cta_counter, 1u);
+        if (prev == gridDim.x - 1u) {
+            atomicExch(p.cta_counter, 0u);
+            fence_acq_rel_sys();
+            mm_red_add_release_u32(p.done_mc, 1u);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+std::once_flag g_attr_once[64];
+
+int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, size_t elem, const void* base, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer, const char* what) {
+    const DriverApi& d = driver();
+    if (!d.ok) return fail(AGG_EDRIVER, "CUDA driver unavailable: %s", d.why.c_str());
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+        return fail(AGG_EINVAL, "%s: base address %p is not 16-byte aligned", what, base);
+    if ((inner * elem) % 16 != 0)
+        return fail(AGG_EINVAL, "%s: row pitch %llu bytes is not a multiple of 16", what,
+                    static_cast<unsigned long long>(inner * elem));
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * elem};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = d.cuTensorMapEncodeTiled(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return check_drv(r, what);
+    return AGG_OK;
+}
+
+int current_sms(int* dev_out) {
+    int dev = 0;
+    AGG_RT(cudaGetDevice(&dev));
+    int sms = 0;
+    AGG_RT(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (dev_out) *dev_out = dev;
+    return sms;
+}
+
+int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    if (!v || !*v) return dflt;
+    return atoi(v);
+}
+
+}  // namespace
+
+int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
+    if (!a) return fail(AGG_EINVAL, "agg_launch: null args");
+    const int world = a->world;
+    const bool f8 = a->dtype == AGG_DTYPE_E4M3;
+    if (a->dtype != AGG_DTYPE_BF16 && !f8) return fail(AGG_EINVAL, "agg_launch: unknown dtype %d", a->dtype);
+    if (world < 1 || world > AGG_MAX_RANKS) return fail(AGG_EINVAL, "agg_launch: world %d", world);
+    if (a->dev_idx < 0 || a->dev_idx >= world) return fail(AGG_EINVAL, "agg_launch: rank %d", a->dev_idx);
+    if (a->M <= 0 || a->N <= 0 || a->K <= 0) return fail(AGG_EINVAL, "agg_launch: empty shape");
+    if (a->M % world) return fail(AGG_EINVAL, "agg_launch: M=%d not divisible by world=%d", a->M, world);
+    const int m_local = a->M / world;
+    const size_t elem = f8 ? 1 : 2;
+    if ((static_cast<size_t>(a->K) * elem) % 16) return fail(AGG_EINVAL, "agg_launch: K*elem must be a multiple of 16");
+    if (a->N % 8) return fail(AGG_EINVAL, "agg_launch: N must be a multiple of 8");
+    if (!a->B || !a->C) return fail(AGG_EINVAL, "agg_launch: null B or C");
+    if (f8 && (!a->scale_a || !a->scale_b)) return fail(AGG_EINVAL, "agg_launch: e4m3 needs scale_a and scale_b");
+    if (world > 1) {
+        if (m_local % BM) return fail(AGG_EINVAL, "agg_launch: M/world=%d must be a multiple of %d", m_local, BM);
+        if (m_local / BM > AGG_MAX_CHUNKS) return fail(AGG_EINVAL, "agg_launch: M/world too large");
+        if (!a->A_local_buf || !a->A_mc || !a->A_copy_ready || !a->A_copy_ready_mc || !a->done_uc || !a->done_mc)
+            return fail(AGG_EINVAL, "agg_launch: multicast buffers missing");
+        if (a->A_copy_epoch < 1) return fail(AGG_EINVAL, "agg_launch: epoch must start at 1");
+    }
+    const void* a_src = a->A_src;
+    if (!a_src) {
+        if (!a->A_local_buf) return fail(AGG_EINVAL, "agg_launch: no A");
+        a_src = static_cast<const uint8_t*>(a->A_local_buf) +
+                static_cast<size_t>(a->dev_idx) * m_local * a->K * elem;
+    }
+
+    int dev = 0;
+    const int sms = current_sms(&dev);
+    if (sms <= 0) return sms < 0 ? sms : fail(AGG_ECUDA, "no SMs");
+
+    KParams p;
+    std::memset(&p, 0, sizeof(p));
+    const CUtensorMapDataType dt = f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint32_t kb_elems = BK_BYTES / static_cast<uint32_t>(elem);
+    int rc;
+    rc = encode_2d(&p.tm_a_src, dt, elem, a_src, a->K, world == 1 ? a->M : m_local, kb_elems, BM, "tensor map A shard");
+    if (rc) return rc;
+    if (world > 1) {
+        rc = encode_2d(&p.tm_a_gath, dt, elem, a->A_local_buf, a->K, a->M, kb_elems, BM, "tensor map gathered A");
+        if (rc) return rc;
+    }
+    rc = encode_2d(&p.tm_b, dt, elem, a->B, a->K, a->N, kb_elems, BN, "tensor map B");
+    if (rc) return rc;
+    rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->C, a->N, a->M, EPI_COLS, EPI_ROWS, "tensor map C");
+    if (rc) return rc;
+
+    p.a_src = static_cast<const uint4*>(a_src);
+    p.M = a->M;
+    p.N = a->N;
+    p.K = a->K;
+    p.rank = a->dev_idx;
+    p.world = world;
+    p.m_local = m_local;
+    p.num_m_tiles = (a->M + BM - 1) / BM;
+    p.num_n_tiles = (a->N + BN - 1) / BN;
+    p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+    p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + BK_BYTES - 1) / BK_BYTES);
+    p.group_m = std::max(1, env_int("AGG_GROUP_M", 16));
+    p.dtype = a->dtype;
+    p.scale_a = a->scale_a;
+    p.scale_b = a->scale_b;
+    p.status = a->status;
+    p.timeout_ns = a->timeout_ns;
+    p.epoch = a->A_copy_epoch;
+
+    const int grid = std::max(1, std::min(sms, p.num_tiles));
+    if (world > 1) {
+        p.a_mc = reinterpret_cast<uint4*>(a->A_mc + static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem);
+        p.shard_bytes = static_cast<unsigned long long>(m_local) * a->K * elem;
+        p.chunk_bytes = static_cast<unsigned long long>(BM) * a->K * elem;
+        // Each chunk is pushed as AGG_PARTS_PER_CHUNK parts, handed to the producer
+        // warps round-robin in chunk order, so early chunks complete first.  The
+        // count is a constant of the protocol: a chunk's flag grows by exactly
+        // AGG_PARTS_PER_CHUNK per launch whatever the grid or shape.
+        const int chunks = m_local / BM;
+        const int ppc = AGG_PARTS_PER_CHUNK;
+        unsigned long long part = (p.chunk_bytes + ppc - 1) / ppc;
+        part = (part + 15) / 16 * 16;
+        p.part_bytes = part;
+        p.ppc = ppc;
+        p.num_parts = chunks * ppc;
+        p.flags_uc = a->A_copy_ready;
+        p.flags_mc = a->A_copy_ready_mc;
+        p.done_uc = a->done_uc;
+        p.done_mc = a->done_mc;
+        p.cta_counter = a->done_uc + 16;
+        if (reinterpret_cast<uintptr_t>(a_src) % 16 || (p.a_mc && reinterpret_cast<uintptr_t>(p.a_mc) % 16))
+            return fail(AGG_EINVAL, "agg_launch: shard pointers must be 16-byte aligned");
+    }
+
+    if (dev >= 0 && dev < 64) {
+        cudaError_t attr_err = cudaSuccess;
+        std::call_once(g_attr_once[dev], [&] {
+            attr_err = cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+        });
+        if (attr_err != cudaSuccess) return check_rt(attr_err, "cudaFuncSetAttribute");
+    } else {
+        AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
+    }
+    ag_gemm_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(p);
+    AGG_RT(cudaGetLastError());
+    return AGG_OK;
+}
+
+}  // namespace agg
+
+extern "C" {
+
+int agg_launch(const agg_args* args, void* stream) {
+    return agg::launch_ag_gemm(args, static_cast<cudaStream_t>(stream));
+}
+
+int agg_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, uint32_t* status,
+                  void* stream) {
+    agg_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.A_src = A;
+    a.B = B;
+    a.C = C;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.world = 1;
+    a.dev_idx = 0;
+    a.A_copy_epoch = 1;
+    a.dtype = AGG_DTYPE_BF16;
+    a.status = status;
+    return agg::launch_ag_gemm(&a, static_cast<cudaStream_t>(stream));
+}
+
+int agg_gemm_e4m3(const void* A, const void* B, void* C, const float* scale_a, const float* scale_b,
+                  int M, int N, int K, uint32_t* status, void* stream) {
+    agg_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.A_src = A;
+    a.B = B;
+    a.C = C;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.world = 1;
+    a.dev_idx = 0;
+    a.A_copy_epoch = 1;
+    a.dtype = AGG_DTYPE_E4M3;
+    a.scale_a = scale_a;
+    a.scale_b = scale_b;
+    a.status = status;
+    return agg::launch_ag_gemm(&a, static_cast<cudaStream_t>(stream));
+}
+
+int agg_num_sms(void) {
+    const int s = agg::current_sms(nullptr);
+    return s > 0 ? s : 0;
+}
+
+}  // extern "C"

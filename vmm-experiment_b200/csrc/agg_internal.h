@@ -1,0 +1,69 @@
+// Host-side internals shared by the library's translation units: the CUDA
+// driver entry points (fetched through the runtime, so libagg.so has no link
+// dependency on libcuda and loads on machines without a GPU driver), and the
+// per-thread error message behind agg_last_error().
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <string>
+
+#include "agg.h"
+
+namespace agg {
+
+#define AGG_DRIVER_FUNCS(X)             \
+    X(cuInit)                           \
+    X(cuGetErrorString)                 \
+    X(cuDeviceGet)                      \
+    X(cuDeviceGetAttribute)             \
+    X(cuMemCreate)                      \
+    X(cuMemRelease)                     \
+    X(cuMemAddressReserve)              \
+    X(cuMemAddressFree)                 \
+    X(cuMemMap)                         \
+    X(cuMemUnmap)                       \
+    X(cuMemSetAccess)                   \
+    X(cuMemGetAllocationGranularity)    \
+    X(cuMemExportToShareableHandle)     \
+    X(cuMemImportFromShareableHandle)   \
+    X(cuMulticastCreate)                \
+    X(cuMulticastAddDevice)             \
+    X(cuMulticastBindMem)               \
+    X(cuMulticastUnbind)                \
+    X(cuMulticastGetGranularity)        \
+    X(cuTensorMapEncodeTiled)
+
+struct DriverApi {
+#define AGG_DECLARE_PFN(name) decltype(&::name) name = nullptr;
+    AGG_DRIVER_FUNCS(AGG_DECLARE_PFN)
+#undef AGG_DECLARE_PFN
+    bool ok = false;
+    std::string why;
+};
+
+// Loads the table once (thread-safe).  ok == false when no driver is present.
+const DriverApi& driver();
+
+// Records a formatted message for agg_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// Helpers that turn CUDA failures into library error codes.
+int check_rt(cudaError_t e, const char* what);
+int check_drv(CUresult r, const char* what);
+
+}  // namespace agg
+
+#define AGG_RT(expr)                                        \
+    do {                                                    \
+        cudaError_t e__ = (expr);                           \
+        if (e__ != cudaSuccess) return ::agg::check_rt(e__, #expr); \
+    } while (0)
+
+#define AGG_DRV(expr)                                       \
+    do {                                                    \
+        CUresult r__ = (expr);                              \
+        if (r__ != CUDA_SUCCESS) return ::agg::check_drv(r__, #expr); \
+    } while (0)
