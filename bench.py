@@ -46,6 +46,9 @@ WORKLOADS = {
     "mlp70b": dict(name="llama3-70b-mlp-gate-up", M=16384, K=8192, N=57344),
     "qkv8b": dict(name="llama3-8b-qkv", M=8192, K=4096, N=6144),
     "smoke": dict(name="smoke-1024", M=1024, K=1024, N=1024),
+    # a 4096-row x 8192-column slice of mlp70b (256 MB of operands): the case
+    # the ncu captures run on
+    "mlp70b_slice": dict(name="llama3-70b-mlp-slice", M=4096, K=8192, N=8192),
 }
 NVLINK_GBS = 770.0        # measured peer copy per direction on this pool
 FALLBACK_HBM_GBS = 6650.0
@@ -95,10 +98,15 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # wait until the sampler is producing lines, so the timed region is covered
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -202,7 +210,7 @@ def cpu_baseline(workload):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mlp70b", choices=sorted(WORKLOADS))
@@ -354,7 +362,7 @@ def main():
         out["e2e"] = {"value": flops_step / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
                       "h2d_bytes_per_step": A_host.numel() * 2, "d2h_bytes_per_step": C_host.numel() * 2,
                       "ms_per_step": ems, "steps": e2e_steps}
-        out["gpu_launches"] = args.steps + e2e_steps
+        out["e2e"]["gpu_launches"] = e2e_steps
         op.check_status()
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -1,0 +1,149 @@
+#pragma once
+// Kernel entry of the harness API.  The reference harness builds a
+// fused_globals<128, 256, 2> and calls launch_ag_gemm_warp_specialized<128, 256,
+// 2, 5>(globals) (vmm/main.cpp:226, 272-296); the types come from an absent
+// submodule.  This header provides the same spellings on top of agg_launch():
+//
+//   dist::local_tensor_from_data_ptr<T>(ptr, b, d, rows, cols)
+//   dist::distributed_tensor_from_data_ptr<T>(mc, peer_addresses, b, d, rows, cols)
+//   ag_gemm_warp_specialized::fused_globals<BM, BN, C>{A, A_local_buf, B, C,
+//       A_copy_ready, A_copy_epoch, dev_idx, M, N}
+//   launch_ag_gemm_warp_specialized<BM, BN, C, S>(globals)
+//
+// Layout the shim maps onto the kernel: `A` describes each rank's shard at the
+// start of its slab (peer_addresses[r] + 0, as vmm/main.cpp:256-258 writes it);
+// the gathered activation is assembled inside the same slab right after the
+// shard, at gather_offset(), and copied into A_local_buf when the launch ends.
+// A_copy_ready is unused: the arrival flags live in the slab's flag area.
+// BM/BN/C/S are accepted for source compatibility; the kernel's tiling is fixed.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <cstring>
+
+#include "agg.h"
+#include "multimem.cuh"
+
+namespace comm {
+using bf16 = __nv_bfloat16;
+}
+
+namespace dist {
+
+template <typename T>
+struct local_tensor {
+    using dtype = T;
+    uint64_t raw_ptr = 0;
+    int b = 1, d = 1, rows = 0, cols = 0;
+    size_t numel() const { return static_cast<size_t>(b) * d * rows * cols; }
+};
+
+template <typename T>
+struct distributed_tensor {
+    using dtype = T;
+    uint64_t mc = 0;
+    const uint64_t* peer_addresses = nullptr;
+    int b = 1, d = 1, rows = 0, cols = 0;
+};
+
+template <typename LT>
+LT local_tensor_from_data_ptr(uint64_t ptr, int b, int d, int rows, int cols) {
+    LT t;
+    t.raw_ptr = ptr;
+    t.b = b;
+    t.d = d;
+    t.rows = rows;
+    t.cols = cols;
+    return t;
+}
+
+template <typename DT>
+DT distributed_tensor_from_data_ptr(uint64_t mc, uint64_t* peers, int b, int d, int rows, int cols) {
+    DT t;
+    t.mc = mc;
+    t.peer_addresses = peers;
+    t.b = b;
+    t.d = d;
+    t.rows = rows;
+    t.cols = cols;
+    return t;
+}
+
+}  // namespace dist
+
+namespace ag_gemm_warp_specialized {
+
+template <int BM, int BN, int C>
+struct fused_globals {
+    using A_distributed_tensor = dist::distributed_tensor<comm::bf16>;
+    using A_local_tensor = dist::local_tensor<comm::bf16>;
+    using B_local_tensor = dist::local_tensor<comm::bf16>;
+    using C_local_tensor = dist::local_tensor<comm::bf16>;
+    A_distributed_tensor A;
+    A_local_tensor A_local_buf;
+    B_local_tensor B;
+    C_local_tensor C;
+    uint32_t* A_copy_ready;
+    uint32_t A_copy_epoch;
+    int dev_idx;
+    int M;
+    int N;
+};
+
+// Offset of the gathered activation inside each slab: after the rank's own
+// shard (rows x cols bf16), rounded to 2 MiB.
+inline size_t gather_offset(size_t shard_bytes) { return (shard_bytes + (2u << 20) - 1) / (2u << 20) * (2u << 20); }
+
+}  // namespace ag_gemm_warp_specialized
+
+template <int BM, int BN, int C, int S>
+int launch_ag_gemm_warp_specialized(const ag_gemm_warp_specialized::fused_globals<BM, BN, C>& g,
+                                    cudaStream_t stream = nullptr) {
+    const int rank = g.dev_idx;
+    const RankState& rs = g_rs[rank];
+    int world = 0;
+    for (int i = 0; i < 8; ++i)
+        if (g.A.peer_addresses && g.A.peer_addresses[i]) world = i + 1;
+    if (world < 1 || !rs.ready) {
+        std::fprintf(stderr, "launch_ag_gemm_warp_specialized: rank %d has no slab\n", rank);
+        return AGG_ESTATE;
+    }
+    const int K = g.A.cols;
+    const int m_local = g.A.rows;
+    const size_t shard_bytes = static_cast<size_t>(m_local) * K * sizeof(comm::bf16);
+    const size_t goff = ag_gemm_warp_specialized::gather_offset(shard_bytes);
+    if (goff + static_cast<size_t>(g.M) * K * sizeof(comm::bf16) > rs.flag_off) {
+        std::fprintf(stderr, "launch_ag_gemm_warp_specialized: gathered A does not fit below the flags\n");
+        return AGG_EINVAL;
+    }
+    agg_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.A_mc = g.A.mc + goff;
+    for (int i = 0; i < world; ++i) a.A_peer[i] = g.A.peer_addresses[i];
+    a.A_local_buf = reinterpret_cast<void*>(rs.uc + goff);
+    a.B = reinterpret_cast<const void*>(g.B.raw_ptr);
+    a.C = reinterpret_cast<void*>(g.C.raw_ptr);
+    a.A_copy_ready = reinterpret_cast<uint32_t*>(rs.uc + rs.flag_off + AGG_FLAG_CHUNK_OFF);
+    a.A_copy_ready_mc = reinterpret_cast<uint32_t*>(rs.mc + rs.flag_off + AGG_FLAG_CHUNK_OFF);
+    a.done_uc = reinterpret_cast<uint32_t*>(rs.uc + rs.flag_off + AGG_FLAG_DONE_OFF);
+    a.done_mc = reinterpret_cast<uint32_t*>(rs.mc + rs.flag_off + AGG_FLAG_DONE_OFF);
+    a.A_copy_epoch = g.A_copy_epoch;
+    a.dev_idx = rank;
+    a.M = g.M;
+    a.N = g.N;
+    a.K = K;
+    a.world = world;
+    a.dtype = AGG_DTYPE_BF16;
+    a.A_src = reinterpret_cast<const void*>(rs.uc);  // the shard at the start of the slab
+    int rc = agg_launch(&a, stream);
+    if (rc != AGG_OK) {
+        std::fprintf(stderr, "launch_ag_gemm_warp_specialized: %s\n", agg_last_error());
+        return rc;
+    }
+    if (g.A_local_buf.raw_ptr && world > 1)
+        cudaMemcpyAsync(reinterpret_cast<void*>(g.A_local_buf.raw_ptr), a.A_local_buf,
+                        static_cast<size_t>(g.M) * K * sizeof(comm::bf16), cudaMemcpyDeviceToDevice, stream);
+    return AGG_OK;
+}
