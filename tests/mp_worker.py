@@ -1,7 +1,11 @@
 """Child-process bodies of the multi-GPU tests (one process per GPU, gloo for
 the host-side rendezvous).  Each function returns a dict of results; the
 parent collects them through a queue.  Kept free of pytest so spawn-started
-children import it cheaply."""
+children import it cheaply.
+
+Every worker ends in _teardown(), also after an exception, so that no rank
+leaves while its slab is still bound to the multicast object and the others
+are still using it."""
 from __future__ import annotations
 
 import datetime
@@ -26,6 +30,27 @@ def _init(rank, world, port):
     return ge.load_package()
 
 
+def _teardown(*objs):
+    """Wait for this GPU's work (every device wait is bounded), meet the other
+    ranks, release the multicast slabs, meet again, leave the group."""
+    import torch
+    import torch.distributed as dist
+
+    try:
+        torch.cuda.synchronize()
+    finally:
+        try:
+            dist.barrier()
+        finally:
+            for o in objs:
+                if o is not None:
+                    o.close()
+            try:
+                dist.barrier()
+            finally:
+                dist.destroy_process_group()
+
+
 def _bits_to_dev(bits, shape):
     import numpy as np
     import torch
@@ -42,32 +67,32 @@ def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme):
     import oracle
 
     pkg = _init(rank, world, port)
-    A_bits, A_ref, B_bits, B_ref = oracle.harness_inputs(world, m_local, k, n_r, scheme)
-    A_r = _bits_to_dev(A_bits[rank], (m_local, k))
-    B_r = _bits_to_dev(B_bits[rank], (n_r, k))
-    op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
-    outs = []
-    for _ in range(launches):
-        C = op(A_r, B_r)
+    op = None
+    try:
+        A_bits, A_ref, B_bits, B_ref = oracle.harness_inputs(world, m_local, k, n_r, scheme)
+        A_r = _bits_to_dev(A_bits[rank], (m_local, k))
+        B_r = _bits_to_dev(B_bits[rank], (n_r, k))
+        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
+        outs = []
+        for _ in range(launches):
+            C = op(A_r, B_r)
+            torch.cuda.synchronize()
+            op.check_status()
+            outs.append(C.clone())
+        gathered = op.gathered().clone()
         torch.cuda.synchronize()
-        op.check_status()
-        outs.append(C.clone())
-    gathered = op.gathered().clone()
-    torch.cuda.synchronize()
-    want_gather = np.concatenate([b.reshape(m_local, k) for b in A_bits]).view(np.int16)
-    gather_ok = bool(np.array_equal(gathered.view(torch.int16).cpu().numpy(), want_gather))
-    full_A = np.concatenate([a.reshape(m_local, k) for a in A_ref])
-    want = oracle.gemm_f64(full_A, B_ref[rank].reshape(n_r, k)).astype(np.float32)
-    got = outs[-1].float().cpu().numpy()
-    stats = oracle.error_stats(got, want)
-    bad, where = oracle.check_close(got, want)
-    same = all(torch.equal(o, outs[0]) for o in outs)
-    dist.barrier()
-    op.close()
-    dist.barrier()
-    dist.destroy_process_group()
-    return {"rank": rank, "gather_ok": gather_ok, "bad": bad, "where": where, "stats": stats,
-            "launches_identical": same, "epoch": op.epoch}
+        want_gather = np.concatenate([b.reshape(m_local, k) for b in A_bits]).view(np.int16)
+        gather_ok = bool(np.array_equal(gathered.view(torch.int16).cpu().numpy(), want_gather))
+        full_A = np.concatenate([a.reshape(m_local, k) for a in A_ref])
+        want = oracle.gemm_f64(full_A, B_ref[rank].reshape(n_r, k)).astype(np.float32)
+        got = outs[-1].float().cpu().numpy()
+        stats = oracle.error_stats(got, want)
+        bad, where = oracle.check_close(got, want)
+        same = all(torch.equal(o, outs[0]) for o in outs)
+        return {"rank": rank, "gather_ok": gather_ok, "bad": bad, "where": where, "stats": stats,
+                "launches_identical": same, "epoch": op.epoch}
+    finally:
+        _teardown(op)
 
 
 def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches):
@@ -78,35 +103,35 @@ def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches):
     import torch.distributed as dist
 
     pkg = _init(rank, world, port)
-    op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
-    g = torch.Generator(device="cuda").manual_seed(rank)
-    B_r = (torch.randn(n_r, k, device="cuda", generator=g) * 0.05).bfloat16()
-    worst = 0.0
-    shards = []
-    outs = []
-    for e in range(launches):
-        ge_ = torch.Generator(device="cuda").manual_seed(100 * e + rank)
-        A_r = torch.randn(m_local, k, device="cuda", generator=ge_).bfloat16()
-        shards.append(A_r)
-        outs.append(op(A_r, B_r))
-    torch.cuda.synchronize()
-    op.check_status()
-    for e in range(launches):
-        parts = []
-        for s in range(world):
-            ge_ = torch.Generator(device="cuda").manual_seed(100 * e + s)
-            parts.append(torch.randn(m_local, k, device="cuda", generator=ge_).bfloat16())
-        ref = torch.cat(parts).float() @ B_r.float().t()
-        err = ((outs[e].float() - ref).abs().max() / ref.abs().max()).item()
-        worst = max(worst, err)
-    dist.barrier()
-    op.close()
-    dist.barrier()
-    dist.destroy_process_group()
-    return {"rank": rank, "worst_rel_err": worst}
+    op = None
+    try:
+        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
+        g = torch.Generator(device="cuda").manual_seed(rank)
+        B_r = (torch.randn(n_r, k, device="cuda", generator=g) * 0.05).bfloat16()
+        outs = []
+        shards = []
+        for e in range(launches):
+            ge_ = torch.Generator(device="cuda").manual_seed(100 * e + rank)
+            A_r = torch.randn(m_local, k, device="cuda", generator=ge_).bfloat16()
+            shards.append(A_r)
+            outs.append(op(A_r, B_r))
+        torch.cuda.synchronize()
+        op.check_status()
+        worst = 0.0
+        for e in range(launches):
+            parts = []
+            for s in range(world):
+                ge_ = torch.Generator(device="cuda").manual_seed(100 * e + s)
+                parts.append(torch.randn(m_local, k, device="cuda", generator=ge_).bfloat16())
+            ref = torch.cat(parts).float() @ B_r.float().t()
+            err = ((outs[e].float() - ref).abs().max() / ref.abs().max()).item()
+            worst = max(worst, err)
+        return {"rank": rank, "worst_rel_err": worst}
+    finally:
+        _teardown(op)
 
 
-def multicast_sweep(rank, world, port, sizes):
+def multicast_sweep(rank, world, port, sizes, reps=1):
     """Each rank pushes `size` bytes into its slot via multimem.st; every rank's
     copy of every slot must be byte-identical to the sender's source."""
     import ctypes
@@ -117,38 +142,43 @@ def multicast_sweep(rank, world, port, sizes):
     pkg = _init(rank, world, port)
     agg = pkg.agg
     L = pkg.lib()
-    maxb = max(sizes)
-    slab = agg.MulticastSlab(rank, world, rank, world * maxb, pkg.agg.make_job_id(), lambda: dist.barrier())
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    bad = torch.zeros(1, dtype=torch.int64, device="cuda")
-    res = []
-    for size in sizes:
-        def src_of(s):
-            g = torch.Generator(device="cuda").manual_seed(7919 * s + size)
-            return (torch.rand(size // 2, device="cuda", generator=g) * 2 - 1).bfloat16()
+    slab = None
+    try:
+        maxb = max(sizes)
+        slab = agg.MulticastSlab(rank, world, rank, world * maxb, agg.make_job_id(), lambda: dist.barrier())
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        bad = torch.zeros(1, dtype=torch.int64, device="cuda")
+        res = []
+        for size in sizes:
+            def src_of(s):
+                g = torch.Generator(device="cuda").manual_seed(7919 * s + size)
+                return (torch.rand(size // 2, device="cuda", generator=g) * 2 - 1).bfloat16()
 
-        src = src_of(rank)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None, 0, stream))
-        e1.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-        agg.check(L.agg_alias_fence(stream))
-        bad.zero_()
-        for s in range(world):
-            exp = src_of(s)
-            agg.check(L.agg_verify_bytes(ctypes.c_void_p(slab.uc + s * size), ctypes.c_void_p(exp.data_ptr()), size,
-                                         ctypes.c_void_p(bad.data_ptr()), stream))
-        torch.cuda.synchronize()
-        res.append({"size": size, "mismatched_words": int(bad.item()), "ms": e0.elapsed_time(e1)})
-    dist.barrier()
-    slab.close()
-    dist.barrier()
-    dist.destroy_process_group()
-    return {"rank": rank, "sweep": res}
+            src = src_of(rank)
+            for _ in range(2):  # warm-up
+                agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None, 0,
+                                             stream))
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None, 0,
+                                             stream))
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            agg.check(L.agg_alias_fence(stream))
+            bad.zero_()
+            for s in range(world):
+                exp = src_of(s)
+                agg.check(L.agg_verify_bytes(ctypes.c_void_p(slab.uc + s * size), ctypes.c_void_p(exp.data_ptr()),
+                                             size, ctypes.c_void_p(bad.data_ptr()), stream))
+            torch.cuda.synchronize()
+            res.append({"size": size, "mismatched_words": int(bad.item()), "ms": e0.elapsed_time(e1) / reps})
+        return {"rank": rank, "sweep": res}
+    finally:
+        _teardown(slab)
 
 
 def multimem_known_answers(rank, world, port):
@@ -163,62 +193,62 @@ def multimem_known_answers(rank, world, port):
     pkg = _init(rank, world, port)
     agg = pkg.agg
     L = pkg.lib()
-    slab = agg.MulticastSlab(rank, world, rank, 1 << 20, pkg.agg.make_job_id(), lambda: dist.barrier())
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rec_off = 4096  # kMulticastTestOffset, include/test_kernel.cuh:9
-    rec = agg.device_view(slab.uc + rec_off, (4,), torch.float32)
-    rec.copy_(torch.tensor([rank + 1.0, 0.0, rank + 1.0, 0.0]))
-    torch.cuda.synchronize()
-    agg.check(L.agg_alias_fence(stream))
-    torch.cuda.synchronize()
-    dist.barrier()
-    reduced = torch.zeros(1, device="cuda")
-    if rank == 0:
-        agg.check(L.agg_multimem_ops_test(slab.mc + rec_off, ctypes.c_void_p(reduced.data_ptr()), 10.0, stream))
+    slab = None
+    try:
+        slab = agg.MulticastSlab(rank, world, rank, 1 << 20, agg.make_job_id(), lambda: dist.barrier())
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rec_off = 4096  # kMulticastTestOffset, include/test_kernel.cuh:9
+        rec = agg.device_view(slab.uc + rec_off, (4,), torch.float32)
+        rec.copy_(torch.tensor([rank + 1.0, 0.0, rank + 1.0, 0.0]))
         torch.cuda.synchronize()
-    dist.barrier()
-    agg.check(L.agg_alias_fence(stream))
-    torch.cuda.synchronize()
-    observed = rec.cpu().tolist()
-    expect_sum = float(sum(r + 1 for r in range(world)))
-    out = {"rank": rank, "store_ok": observed[1] == expect_sum, "red_ok": observed[2] == rank + 1.0 + 10.0,
-           "reduce_ok": (rank != 0) or float(reduced.item()) == expect_sum, "observed": observed}
-
-    # vector ld_reduce / red over 1024 float4s
-    n4 = 1024
-    base = slab.uc + (64 << 10)
-    vec = agg.device_view(base, (4 * n4,), torch.float32)
-    vec.copy_(torch.arange(4 * n4, device="cuda", dtype=torch.float32) * (rank + 1))
-    torch.cuda.synchronize()
-    dist.barrier()
-    summed = torch.zeros(4 * n4, device="cuda")
-    agg.check(L.agg_multimem_ld_reduce_v4(slab.mc + (64 << 10), ctypes.c_void_p(summed.data_ptr()), n4, stream))
-    torch.cuda.synchronize()
-    dist.barrier()
-    agg.check(L.agg_multimem_red_add_v4(slab.mc + (64 << 10), 1.0, n4, stream))
-    torch.cuda.synchronize()
-    dist.barrier()
-    agg.check(L.agg_alias_fence(stream))
-    torch.cuda.synchronize()
-    w = float(sum(r + 1 for r in range(world)))
-    ar = np.arange(4 * n4, dtype=np.float32)
-    out["ld_reduce_ok"] = bool(np.array_equal(summed.cpu().numpy(), ar * w))
-    out["red_v4_ok"] = bool(np.array_equal(vec.cpu().numpy(), ar * (rank + 1) + world))
-
-    # mm_barrier: every CTA of every rank adds 1 on all GPUs; wait for `world`
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    for it in (1, 2):
-        agg.check(L.agg_mm_barrier(ctypes.c_void_p(slab.user(mc=True)), ctypes.c_void_p(slab.user()), 0,
-                                   it * world, 8, ctypes.c_void_p(status.data_ptr()), 5_000_000_000, stream))
+        agg.check(L.agg_alias_fence(stream))
         torch.cuda.synchronize()
-    out["barrier_status"] = int(status.item())
-    flags = agg.device_view(slab.user(), (8,), torch.int32).cpu().tolist()
-    out["barrier_flags_ok"] = flags == [2 * world] * 8
-    dist.barrier()
-    slab.close()
-    dist.barrier()
-    dist.destroy_process_group()
-    return out
+        dist.barrier()
+        reduced = torch.zeros(1, device="cuda")
+        if rank == 0:
+            agg.check(L.agg_multimem_ops_test(slab.mc + rec_off, ctypes.c_void_p(reduced.data_ptr()), 10.0, stream))
+            torch.cuda.synchronize()
+        dist.barrier()
+        agg.check(L.agg_alias_fence(stream))
+        torch.cuda.synchronize()
+        observed = rec.cpu().tolist()
+        expect_sum = float(sum(r + 1 for r in range(world)))
+        out = {"rank": rank, "store_ok": observed[1] == expect_sum, "red_ok": observed[2] == rank + 1.0 + 10.0,
+               "reduce_ok": (rank != 0) or float(reduced.item()) == expect_sum, "observed": observed}
+
+        # vector ld_reduce / red over 1024 float4s
+        n4 = 1024
+        voff = 64 << 10
+        vec = agg.device_view(slab.uc + voff, (4 * n4,), torch.float32)
+        vec.copy_(torch.arange(4 * n4, device="cuda", dtype=torch.float32) * (rank + 1))
+        torch.cuda.synchronize()
+        dist.barrier()
+        summed = torch.zeros(4 * n4, device="cuda")
+        agg.check(L.agg_multimem_ld_reduce_v4(slab.mc + voff, ctypes.c_void_p(summed.data_ptr()), n4, stream))
+        torch.cuda.synchronize()
+        dist.barrier()
+        agg.check(L.agg_multimem_red_add_v4(slab.mc + voff, 1.0, n4, stream))
+        torch.cuda.synchronize()
+        dist.barrier()
+        agg.check(L.agg_alias_fence(stream))
+        torch.cuda.synchronize()
+        w = float(sum(r + 1 for r in range(world)))
+        ar = np.arange(4 * n4, dtype=np.float32)
+        out["ld_reduce_ok"] = bool(np.array_equal(summed.cpu().numpy(), ar * w))
+        out["red_v4_ok"] = bool(np.array_equal(vec.cpu().numpy(), ar * (rank + 1) + world))
+
+        # mm_barrier: every CTA of every rank adds 1 on all GPUs; wait for it * world
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for it in (1, 2):
+            agg.check(L.agg_mm_barrier(ctypes.c_void_p(slab.user(mc=True)), ctypes.c_void_p(slab.user()), 0,
+                                       it * world, 8, ctypes.c_void_p(status.data_ptr()), 5_000_000_000, stream))
+            torch.cuda.synchronize()
+        out["barrier_status"] = int(status.item())
+        flags = agg.device_view(slab.user(), (8,), torch.int32).cpu().tolist()
+        out["barrier_flags_ok"] = flags == [2 * world] * 8
+        return out
+    finally:
+        _teardown(slab)
 
 
 def run_child(fn_name, rank, world, port, q, kwargs):

@@ -104,6 +104,20 @@ namespace {
 
 size_t round_up(size_t x, size_t g) { return (x + g - 1) / g * g; }
 
+// Makes `device`'s primary context current for the driver calls of one entry
+// point and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
 CUmemAllocationProp phys_prop(int device) {
     CUmemAllocationProp ap;
     std::memset(&ap, 0, sizeof(ap));
@@ -524,6 +538,8 @@ int agg_mp_open(int rank, int world, int device, size_t data_bytes, const char* 
     if (rank < 0 || world < 1 || world > AGG_MAX_RANKS || rank >= world)
         return fail(AGG_EINVAL, "agg_mp_open: rank %d / world %d", rank, world);
     DRV_OR_FAIL();
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(AGG_ECUDA, "agg_mp_open: cannot select device %d", device);
     int rc = check_multicast_supported(device);
     if (rc) return rc;
     agg_mp_ctx* c = new agg_mp_ctx();
@@ -632,6 +648,7 @@ int agg_mp_add_device(agg_mp_ctx* c) {
     if (!c || !c->exchanged) return fail(AGG_ESTATE, "agg_mp_add_device: exchange first");
     if (c->added) return AGG_OK;
     DRV_OR_FAIL();
+    DeviceGuard guard(c->device);
     if (c->rank != 0) {
         AGG_DRV(D.cuMemImportFromShareableHandle(&c->mc, reinterpret_cast<void*>(static_cast<uintptr_t>(c->mc_fd)),
                                                   CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR));
@@ -647,9 +664,7 @@ int agg_mp_bind(agg_mp_ctx* c, agg_rank_info* out) {
     if (!c || !c->added) return fail(AGG_ESTATE, "agg_mp_bind: add_device and a barrier first");
     DRV_OR_FAIL();
     if (!c->bound) {
-        int prev = 0;
-        AGG_RT(cudaGetDevice(&prev));
-        AGG_RT(cudaSetDevice(c->device));
+        DeviceGuard guard(c->device);
         AGG_DRV(D.cuMulticastBindMem(c->mc, 0, c->phys, 0, c->slab, 0));
         int rc = map_range(&c->uc, c->slab, c->phys, &c->device, 1);
         if (rc) return rc;
@@ -668,7 +683,6 @@ int agg_mp_bind(agg_mp_ctx* c, agg_rank_info* out) {
         }
         rc = zero_flags(c->uc, c->flag_off, c->device);
         if (rc) return rc;
-        cudaSetDevice(prev);
         c->bound = true;
     }
     fill_info(out, c->rank, c->world, c->device, c->uc, c->mcva, c->peer_uc, c->slab, c->flag_off);
@@ -679,6 +693,8 @@ int agg_mp_close(agg_mp_ctx* c) {
     if (!c) return AGG_OK;
     const DriverApi& D = driver();
     if (D.ok) {
+        DeviceGuard guard(c->device);
+        cudaDeviceSynchronize();  // nothing of ours may still touch the mappings
         for (int p = 0; p < c->world && p < AGG_MAX_RANKS; ++p) {
             if (p != c->rank && c->peer_uc[p]) unmap_range(c->peer_uc[p], c->slab);
             if (c->peer_phys[p]) D.cuMemRelease(c->peer_phys[p]);
