@@ -217,6 +217,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-unfused", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="multicast write bandwidth sweep (1 MiB .. --sweep-max) instead of the GEMM")
+    ap.add_argument("--sweep-max", type=int, default=1 << 30)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -244,6 +247,32 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+
+    if args.sweep:
+        if world < 2:
+            raise SystemExit("--sweep needs torchrun with 2 or more ranks")
+        import importlib
+
+        sweep = importlib.import_module(pkg.__name__ + ".sweep")
+        sizes = []
+        s = 1 << 20
+        while s <= args.sweep_max:
+            sizes.append(s)
+            s <<= 1
+        slab = pkg.agg.MulticastSlab(rank, world, local_rank, world * sizes[-1], pkg.agg.make_job_id(host_group),
+                                     lambda: dist.barrier(group=host_group))
+        try:
+            rows = sweep.run(slab, sizes, reps=args.steps, warmup=args.warmup, group=host_group)
+        finally:
+            torch.cuda.synchronize()
+            dist.barrier(group=host_group)
+            slab.close()
+            dist.barrier(group=host_group)
+        if rank == 0:
+            print(json.dumps({"sweep": "multicast multimem.st write bandwidth", "n_gpus": world, "unit": "GB/s",
+                              "rows": rows}), flush=True)
+        dist.destroy_process_group()
+        return
 
     w = WORKLOADS[args.workload]
     M, K, Ntot = w["M"], w["K"], w["N"]

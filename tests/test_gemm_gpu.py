@@ -14,6 +14,23 @@ pytestmark = pytest.mark.gpu
 
 MAX_REL = 1e-2
 
+# Kernel variants selectable at launch time: the one-CTA kernel (128 x 256 tiles)
+# and the CTA-pair kernel (256 x 256 or 256 x 128 tiles).
+VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
+            "pair256": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_STAGES": "6"},
+            "pair256s7": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_STAGES": "7"},
+            "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_STAGES": "8"},
+            "pair128s9": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_STAGES": "9"}}
+
+
+@pytest.fixture(params=sorted(VARIANTS))
+def variant(request, monkeypatch):
+    for k in ("AGG_KERNEL", "AGG_BN", "AGG_STAGES"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in VARIANTS[request.param].items():
+        monkeypatch.setenv(k, v)
+    return request.param
+
 
 def to_dev_bf16(bits, shape):
     import torch
@@ -48,7 +65,7 @@ def check_against(oracle, got, want):
     (77, 1000, 40),      # K shorter than one k-block
     (640, 768, 4096),    # several waves of k-blocks, N not a multiple of 256
 ])
-def test_gemm_matches_oracle(pkg, oracle, gpu, M, N, K):
+def test_gemm_matches_oracle(pkg, oracle, gpu, variant, M, N, K):
     a_bits, a_ref = oracle.fill_random_bf16(1, M * K)
     b_bits, b_ref = oracle.fill_random_bf16(2, N * K)
     C = run_gemm(pkg, to_dev_bf16(a_bits, (M, K)), to_dev_bf16(b_bits, (N, K)))
@@ -56,7 +73,7 @@ def test_gemm_matches_oracle(pkg, oracle, gpu, M, N, K):
     check_against(oracle, C.float().cpu().numpy(), want)
 
 
-def test_gemm_matches_reference_cublas_path(pkg, oracle, gpu):
+def test_gemm_matches_reference_cublas_path(pkg, oracle, gpu, variant):
     """The reference's own reference_matmul_cublas + check_close (oracle/_ref)."""
     R = oracle.ref_lib()
     if R is None:
@@ -75,7 +92,7 @@ def test_gemm_matches_reference_cublas_path(pkg, oracle, gpu):
     check_against(oracle, got, want)
 
 
-def test_gemm_matches_torch_fp32(pkg, gpu):
+def test_gemm_matches_torch_fp32(pkg, gpu, variant):
     import torch
 
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -88,7 +105,7 @@ def test_gemm_matches_torch_fp32(pkg, gpu):
     assert err <= MAX_REL, err
 
 
-def test_repeated_launches_are_identical(pkg, gpu):
+def test_repeated_launches_are_identical(pkg, gpu, variant):
     import torch
 
     g = torch.Generator(device="cuda").manual_seed(9)
@@ -120,11 +137,11 @@ def sampled_check(pkg, oracle, M, N, K, seed):
     assert torch.isfinite(C).all().item()
 
 
-def test_gemm_llama8b_qkv_shape_sampled(pkg, oracle, gpu):
+def test_gemm_llama8b_qkv_shape_sampled(pkg, oracle, gpu, variant):
     sampled_check(pkg, oracle, 8192, 6144, 4096, 11)
 
 
-def test_gemm_llama70b_mlp_shape_sampled(pkg, oracle, gpu):
+def test_gemm_llama70b_mlp_shape_sampled(pkg, oracle, gpu, variant):
     # one rank's share at P=8 (N_r = 57344 / 8)
     sampled_check(pkg, oracle, 16384, 7168, 8192, 12)
 

@@ -43,6 +43,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <string>
 
 #include "agg.h"
 #include "agg_internal.h"
@@ -96,6 +97,7 @@ struct alignas(64) KParams {
     uint32_t* cta_counter;
     const float* scale_a;
     const float* scale_b;
+    void* c_ptr;  // C, for the epilogue that stores without TMA
     uint32_t* status;
     unsigned long long timeout_ns;
     uint32_t epoch;
@@ -106,12 +108,13 @@ struct alignas(64) KParams {
     int ppc, num_parts;
     int group_m;
     int dtype;
+    int tile_m;  // rows per m-tile: 128 (one CTA) or 256 (a CTA pair)
 };
 
 // Position `pos` of the m-tile visiting order -> global m-tile index.
 __device__ __forceinline__ int m_tile_at(const KParams& p, int pos) {
     if (p.world == 1) return pos;
-    const int L = p.m_local / BM;
+    const int L = p.m_local / p.tile_m;
     if (pos < L) return p.rank * L + pos;
     const int q = pos - L;
     const int c = q / (p.world - 1);
@@ -278,7 +281,7 @@ __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, u
         int mt, nt;
         tile_coords(p, t, mt, nt);
         int got = 1;
-        if (lane == 0) got = mbar_wait(&tfull[acc], acc_phase, dl) ? 1 : 0;
+        if (lane == 0) got = mbar_wait_sleepy(&tfull[acc], acc_phase, dl) ? 1 : 0;
         got = __shfl_sync(0xffffffffu, got, 0);
         if (!got) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, static_cast<uint32_t>(t));
@@ -482,10 +485,360 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
     }
 }
 
+// ================================================================ CTA-pair kernel
+//
+// The same roles on a cluster of two CTAs that share one tcgen05.mma.cta_group::2
+// per k-step: the pair computes a 256 x BN tile, each CTA holding 128 rows of A
+// and BN/2 rows of B in its shared memory and 128 x BN accumulators in its TMEM.
+// Per SM that halves the B traffic from L2 and the smem bytes the tensor core
+// reads per FLOP, and frees room for 6 (BN=256) or 8 (BN=128) pipeline stages.
+//
+//   both CTAs   loader: waits on its own `empty` barrier, TMA-loads its A half
+//               and B half, completion counted on the EVEN CTA's `full` barrier
+//               (the even CTA arms it with both CTAs' bytes);
+//   even CTA    MMA issuer: waits `full`, issues the pair MMA, commits to
+//               `empty` in both CTAs, and to `tfull` in both CTAs per tile;
+//   both CTAs   epilogue: drains its own TMEM, arrives on the even CTA's `tempty`.
+template <int BN2, int ST>
+struct PairCfg {
+    static constexpr int TILE_M = 256;
+    static constexpr int B_ROWS = BN2 / 2;
+    static constexpr int A_BYTES = 128 * BK_BYTES;
+    static constexpr int B_BYTES = B_ROWS * BK_BYTES;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGES = ST;
+    static constexpr int EPI_OFF = STAGES * STAGE;
+    // The epilogue stages C through swizzled smem for TMA stores when there is
+    // room; with one stage more it writes 16-byte row segments straight to HBM.
+    static constexpr bool STAGED_EPI = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES + 256 + 1024 <= 232448;
+    static constexpr int BAR_OFF = EPI_OFF + (STAGED_EPI ? EPI_WARPS * 2 * EPI_BUF_BYTES : 0);
+    static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+    static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
+    static constexpr int SMEM = SLOT_OFF + 16 + 1024;
+    static constexpr uint32_t TMEM_COLS = 2 * BN2;  // two accumulators: 512 or 256 columns
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle alignment");
+    static_assert(STAGES <= 32, "stage masks are 32-bit");
+};
+
+template <int BN2, int ST>
+__device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                            uint32_t crank, const Deadline& dl) {
+    using G = PairCfg<BN2, ST>;
+    tma_prefetch_desc(&p.tm_a_src);
+    tma_prefetch_desc(&p.tm_b);
+    if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
+    const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used = 0, last_par = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        const int row = mt * G::TILE_M + static_cast<int>(crank) * 128;  // this CTA's first row of gathered A
+        const CUtensorMap* tma = &p.tm_a_src;
+        int a_row = row;
+        if (p.world > 1) {
+            const int src = row / p.m_local;
+            if (src == p.rank) {
+                a_row = row - src * p.m_local;
+            } else {
+                const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (row - src * p.m_local) / BM;
+                if (!wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl)) {
+                    record_failure(p.status, AGG_ROLE_FLAG, static_cast<uint32_t>(row / BM));
+                    ok = false;
+                    break;
+                }
+                fence_proxy_alias();
+                fence_proxy_async_global();
+                tma = &p.tm_a_gath;
+            }
+        }
+        const int b_row = nt * BN2 + static_cast<int>(crank) * G::B_ROWS;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, dl)) {
+                record_failure(p.status, AGG_ROLE_TMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            uint8_t* sa = smem + stage * G::STAGE;
+            uint8_t* sb = sa + G::A_BYTES;
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE);
+            const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(tma, sa, bar, kb * kb_elems, a_row);
+            tma_load_2d_pair(&p.tm_b, sb, bar, kb * kb_elems, b_row);
+            used |= 1u << stage;
+            last_par = (last_par & ~(1u << stage)) | (phase << stage);
+            if (++stage == G::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+    // The even CTA's `full` barriers count both CTAs' bytes of every phase it armed.
+    if (crank == 0)
+        for (int s = 0; s < G::STAGES; ++s)
+            if (used & (1u << s))
+                if (!mbar_wait_for(&full[s], (last_par >> s) & 1u, 200000000ull))
+                    record_failure(p.status, AGG_ROLE_DRAIN, 1u);
+}
+
+template <int BN2, int ST>
+__device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                         const Deadline& dl) {
+    using G = PairCfg<BN2, ST>;
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, BN2) : make_idesc(1, 1, G::TILE_M, BN2);
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, dl)) {
+            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+            break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait(&full[stage], phase, dl)) {
+                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + stage * G::STAGE);
+            const uint64_t adesc = sw128_kmajor_desc(sa);
+            const uint64_t bdesc = sw128_kmajor_desc(sa + G::A_BYTES);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t off = static_cast<uint64_t>(k * 2);
+                const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+                if (f8)
+                    umma_f8_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                else
+                    umma_f16_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+            }
+            umma_commit_pair_mc(&empty[stage], 0x3);
+            if (++stage == G::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tfull[acc], 0x3);
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+    umma_commit_pair_mc(drain, 0x1);
+    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+}
+
+template <int BN2, int ST>
+__device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
+                                              uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
+    using G = PairCfg<BN2, ST>;
+    const int eg = warp & 3;
+    const uint32_t lane = lane_id();
+    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        int got = 1;
+        if (lane == 0) got = mbar_wait_sleepy(&tfull[acc], acc_phase, dl) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, static_cast<uint32_t>(t));
+            break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + static_cast<uint32_t>(acc * BN2);
+        const int row0 = mt * G::TILE_M + static_cast<int>(crank) * 128 + eg * 32;
+        float row_scale = 1.0f;
+        if (f8) {
+            const int row = row0 + static_cast<int>(lane);
+            row_scale = row < p.M ? __ldg(p.scale_a + row) : 0.0f;
+        }
+#pragma unroll 1
+        for (int j = 0; j < BN2 / EPI_COLS; ++j) {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS), r0);
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS + 32), r1);
+            tmem_wait_ld();
+            const int col0 = nt * BN2 + j * EPI_COLS;
+            uint32_t packed[32];
+            if (f8) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]) * row_scale * s0,
+                                            __uint_as_float(r0[2 * i + 1]) * row_scale * s1);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 32 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]) * row_scale * s0,
+                                                 __uint_as_float(r1[2 * i + 1]) * row_scale * s1);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+            }
+            if (j == BN2 / EPI_COLS - 1) {
+                // Every TMEM read of this accumulator is done: hand it back to the
+                // MMA issuer before the last stores go out.
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+            }
+            if constexpr (G::STAGED_EPI) {
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                uint8_t* b = stg + buf * EPI_BUF_BYTES;
+                const uint32_t row_base = smem_u32(b) + lane * 128u;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t addr = row_base + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * c]),
+                                 "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
+                                 : "memory");
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&p.tm_c, b, col0, row0);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            } else {
+                // One row per thread, 16-byte segments straight to global memory.
+                const int row = row0 + static_cast<int>(lane);
+                if (row < p.M) {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.c_ptr) +
+                                                          static_cast<size_t>(row) * p.N + col0);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        if (col0 + 8 * c < p.N)
+                            __stcs(dst + c, make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                                       packed[4 * c + 3]));
+                }
+            }
+        }
+        if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+}
+
+template <int BN2, int ST>
+__global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __grid_constant__ KParams p) {
+    using G = PairCfg<BN2, ST>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::BAR_OFF);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + G::STAGES;
+    uint64_t* tfull = bars + 2 * G::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::SLOT_OFF);
+
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const uint32_t lane = lane_id();
+    const uint32_t crank = cluster_ctarank();
+    Deadline dl;
+    dl.end_ns = globaltimer_ns() + (p.timeout_ns ? p.timeout_ns : 10000000000ull);
+    dl.status = p.status;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        fence_mbarrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, G::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or complete_tx
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+    if (warp == 0) {
+        if (lane == 0) pair_loader<BN2, ST>(p, smem, full, empty, crank, dl);
+    } else if (warp == 1) {
+        if (lane == 0 && crank == 0) pair_mma<BN2, ST>(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        __syncwarp();
+    } else if (warp < 2 + EPI_WARPS) {
+        pair_epilogue<BN2, ST>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+    } else if (p.world > 1) {
+        role_producer(p, warp - 2 - EPI_WARPS, dl);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (failed(p.status)) {
+        // A role gave up: let copies the peer CTA issued toward this CTA land
+        // before the pair dissolves.
+        const uint64_t until = globaltimer_ns() + 2000000ull;
+        while (globaltimer_ns() < until) {
+        }
+    }
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, G::TMEM_COLS);
+    }
+    if (p.world > 1 && threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t prev = atomicAdd(p.cta_counter, 1u);
+        if (prev == gridDim.x - 1u) {
+            atomicExch(p.cta_counter, 0u);
+            fence_acq_rel_sys();
+            mm_red_add_release_u32(p.done_mc, 1u);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- host side
 namespace {
-
-std::once_flag g_attr_once[64];
 
 int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, size_t elem, const void* base, uint64_t inner,
               uint64_t outer, uint32_t box_inner, uint32_t box_outer, const char* what) {
@@ -525,6 +878,86 @@ int env_int(const char* name, int dflt) {
 
 }  // namespace
 
+namespace {
+
+// The CTA-pair kernel instantiations: tile width x pipeline depth.  The deeper
+// variant of each width trades the epilogue's smem staging for one more stage.
+struct PairKernel {
+    const void* fn;
+    int smem;
+    int bn;
+    int stages;
+    bool staged_epilogue;
+    int clusters;  // resident CTA pairs on this device
+};
+
+template <int BN2, int ST>
+PairKernel pair_kernel_entry() {
+    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<BN2, ST>), PairCfg<BN2, ST>::SMEM, BN2, ST,
+                      PairCfg<BN2, ST>::STAGED_EPI, 0};
+}
+
+constexpr int kNumPairKernels = 4;
+
+// Per-device launch facts, filled once: SM count and how many CTA pairs of each
+// pair kernel can be resident at once (clusters must fit inside a GPC).
+struct DevInfo {
+    int sms = 0;
+    PairKernel pair[kNumPairKernels];
+    int rc = AGG_OK;
+    std::string err;
+};
+DevInfo g_dev[64];
+std::once_flag g_dev_once[64];
+
+int max_pair_clusters(const void* kern, int smem, int sms, int* out) {
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    AGG_RT(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    *out = n;
+    return AGG_OK;
+}
+
+int device_info(int dev, const DevInfo** out) {
+    if (dev < 0 || dev >= 64) return fail(AGG_EINVAL, "device ordinal %d out of range", dev);
+    std::call_once(g_dev_once[dev], [dev] {
+        DevInfo& d = g_dev[dev];
+        d.pair[0] = pair_kernel_entry<256, 6>();
+        d.pair[1] = pair_kernel_entry<256, 7>();
+        d.pair[2] = pair_kernel_entry<128, 8>();
+        d.pair[3] = pair_kernel_entry<128, 9>();
+        auto setup = [&]() -> int {
+            AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+            AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
+            for (PairKernel& k : d.pair) {
+                AGG_RT(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem));
+                int rc = max_pair_clusters(k.fn, k.smem, d.sms, &k.clusters);
+                if (rc) return rc;
+            }
+            return AGG_OK;
+        };
+        d.rc = setup();
+        if (d.rc) d.err = agg_last_error();
+    });
+    if (g_dev[dev].rc) return fail(g_dev[dev].rc, "kernel setup failed: %s", g_dev[dev].err.c_str());
+    *out = &g_dev[dev];
+    return AGG_OK;
+}
+
+
+}  // namespace
+
 int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     if (!a) return fail(AGG_EINVAL, "agg_launch: null args");
     const int world = a->world;
@@ -555,37 +988,61 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     }
 
     int dev = 0;
-    const int sms = current_sms(&dev);
-    if (sms <= 0) return sms < 0 ? sms : fail(AGG_ECUDA, "no SMs");
+    AGG_RT(cudaGetDevice(&dev));
+    const DevInfo* di = nullptr;
+    int rc = device_info(dev, &di);
+    if (rc) return rc;
+
+    // ---- kernel choice: the CTA-pair kernel unless the shard height forbids it.
+    // Tile width 256 unless that leaves fewer than two waves of tiles; the
+    // deeper pipeline variant (AGG_STAGES) for A/B measurement.
+    const PairKernel* pk = nullptr;
+    const char* kenv = getenv("AGG_KERNEL");
+    const bool force_1sm = kenv && std::strcmp(kenv, "1sm") == 0;
+    if (!force_1sm && !(world > 1 && m_local % 256) && di->pair[0].clusters >= 1) {
+        const int bn_env = env_int("AGG_BN", 0);
+        const long tiles256 = static_cast<long>((a->M + 255) / 256) * ((a->N + 255) / 256);
+        int bn = 256;
+        if (bn_env == 128 || (bn_env == 0 && (a->N <= 128 || tiles256 < 2L * di->pair[0].clusters))) bn = 128;
+        const int st_env = env_int("AGG_STAGES", 0);
+        for (const PairKernel& k : di->pair)
+            if (k.bn == bn && (st_env ? k.stages == st_env : k.staged_epilogue)) pk = &k;
+        if (!pk) return fail(AGG_EINVAL, "agg_launch: no pair kernel with BN=%d and %d stages", bn, st_env);
+        if (pk->clusters < 1) pk = nullptr;
+    }
+    const int tile_m = pk ? 256 : BM;
+    const int tile_n = pk ? pk->bn : BN;
+    const int b_box = pk ? tile_n / 2 : BN;
 
     KParams p;
     std::memset(&p, 0, sizeof(p));
     const CUtensorMapDataType dt = f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const uint32_t kb_elems = BK_BYTES / static_cast<uint32_t>(elem);
-    int rc;
     rc = encode_2d(&p.tm_a_src, dt, elem, a_src, a->K, world == 1 ? a->M : m_local, kb_elems, BM, "tensor map A shard");
     if (rc) return rc;
     if (world > 1) {
         rc = encode_2d(&p.tm_a_gath, dt, elem, a->A_local_buf, a->K, a->M, kb_elems, BM, "tensor map gathered A");
         if (rc) return rc;
     }
-    rc = encode_2d(&p.tm_b, dt, elem, a->B, a->K, a->N, kb_elems, BN, "tensor map B");
+    rc = encode_2d(&p.tm_b, dt, elem, a->B, a->K, a->N, kb_elems, static_cast<uint32_t>(b_box), "tensor map B");
     if (rc) return rc;
     rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->C, a->N, a->M, EPI_COLS, EPI_ROWS, "tensor map C");
     if (rc) return rc;
 
     p.a_src = static_cast<const uint4*>(a_src);
+    p.c_ptr = a->C;
     p.M = a->M;
     p.N = a->N;
     p.K = a->K;
     p.rank = a->dev_idx;
     p.world = world;
     p.m_local = m_local;
-    p.num_m_tiles = (a->M + BM - 1) / BM;
-    p.num_n_tiles = (a->N + BN - 1) / BN;
+    p.tile_m = tile_m;
+    p.num_m_tiles = (a->M + tile_m - 1) / tile_m;
+    p.num_n_tiles = (a->N + tile_n - 1) / tile_n;
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
     p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + BK_BYTES - 1) / BK_BYTES);
-    p.group_m = std::max(1, env_int("AGG_GROUP_M", 16));
+    p.group_m = std::max(1, env_int("AGG_GROUP_M", pk ? 8 : 16));
     p.dtype = a->dtype;
     p.scale_a = a->scale_a;
     p.scale_b = a->scale_b;
@@ -593,7 +1050,6 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.timeout_ns = a->timeout_ns;
     p.epoch = a->A_copy_epoch;
 
-    const int grid = std::max(1, std::min(sms, p.num_tiles));
     if (world > 1) {
         p.a_mc = reinterpret_cast<uint4*>(a->A_mc + static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem);
         p.shard_bytes = static_cast<unsigned long long>(m_local) * a->K * elem;
@@ -618,17 +1074,28 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
             return fail(AGG_EINVAL, "agg_launch: shard pointers must be 16-byte aligned");
     }
 
-    if (dev >= 0 && dev < 64) {
-        cudaError_t attr_err = cudaSuccess;
-        std::call_once(g_attr_once[dev], [&] {
-            attr_err = cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
-        });
-        if (attr_err != cudaSuccess) return check_rt(attr_err, "cudaFuncSetAttribute");
-    } else {
-        AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
+    if (!pk) {
+        const int grid = std::max(1, std::min(di->sms, p.num_tiles));
+        ag_gemm_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(p);
+        AGG_RT(cudaGetLastError());
+        return AGG_OK;
     }
-    ag_gemm_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(p);
-    AGG_RT(cudaGetLastError());
+    const int clusters = std::max(1, std::min(pk->clusters, p.num_tiles));
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(pk->smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* kargs[] = {&p};
+    AGG_RT(cudaLaunchKernelExC(&cfg, pk->fn, kargs));
     return AGG_OK;
 }
 
