@@ -133,7 +133,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ reference arm
-def run_reference(args, rank):
+def run_reference(args, rank, emit):
     if rank != 0:
         return
     import numpy as np
@@ -166,7 +166,7 @@ def run_reference(args, rank):
         "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 METRIC = "all-gather GEMM TFLOP/s per GPU at 1/2/4/8 B200; % of roofline; vs NCCL+cuBLAS"
@@ -220,8 +220,18 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="multicast write bandwidth sweep (1 MiB .. --sweep-max) instead of the GEMM")
     ap.add_argument("--sweep-max", type=int, default=1 << 30)
+    ap.add_argument("--trace", default=None, metavar="PATH",
+                    help="after timing, trace one launch per rank and write the per-event summary to PATH")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    # Library banners (NCCL, ...) go to stderr: stdout carries only the result line.
+    sys.stdout.flush()
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(obj):
+        sys.stdout.flush()
+        os.write(result_fd, (json.dumps(obj) + "\n").encode())
 
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
@@ -230,7 +240,7 @@ def main():
         args.gpus = world
 
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, emit)
         return
 
     import datetime
@@ -269,8 +279,8 @@ def main():
             slab.close()
             dist.barrier(group=host_group)
         if rank == 0:
-            print(json.dumps({"sweep": "multicast multimem.st write bandwidth", "n_gpus": world, "unit": "GB/s",
-                              "rows": rows}), flush=True)
+            emit({"sweep": "multicast multimem.st write bandwidth", "n_gpus": world, "unit": "GB/s",
+                  "rows": rows})
         dist.destroy_process_group()
         return
 
@@ -397,9 +407,27 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.workload)
 
+    if args.trace:
+        # one more launch, outside every timed region, with the event trace on
+        tr = op.new_trace()
+        torch.cuda.synchronize()
+        barrier()
+        op(A_r, B_r, out=C_r, trace=tr)
+        torch.cuda.synchronize()
+        op.check_status()
+        rows = tr.cpu().numpy()
+        per_rank = [rows]
+        if world > 1:
+            per_rank = [None] * world
+            dist.all_gather_object(per_rank, rows, group=host_group)
+        if rank == 0:
+            with open(args.trace, "w") as f:
+                json.dump({"workload": config_of(args.workload, world),
+                           "ranks": [pkg.agg.trace_summary(r) for r in per_rank]}, f, indent=1)
+
     op.close()
     if rank == 0:
-        print(json.dumps(out), flush=True)
+        emit(out)
     if world > 1:
         barrier()
         dist.destroy_process_group()

@@ -126,7 +126,25 @@ typedef struct agg_args {
     const float* scale_b;          /* e4m3: per-row scale of B_r [N_r] (per output column) */
     uint32_t* status;              /* device status word (AGG_STATUS_*), may be NULL */
     uint64_t timeout_ns;           /* bound on every device-side wait; 0 = 10 s */
+    uint64_t* trace;               /* optional: u64 [grid][AGG_TRACE_SLOTS] event times (ns) */
 } agg_args;
+
+/* Per-CTA trace slots written when agg_args.trace is not NULL (%globaltimer, ns;
+   0 = event did not happen).  The grid never exceeds agg_num_sms() CTAs, so a
+   buffer of agg_num_sms() * AGG_TRACE_SLOTS u64 (zeroed) always suffices. */
+#define AGG_TRACE_SLOTS 16
+#define AGG_TR_START 0          /* CTA start                                          */
+#define AGG_TR_PROD_GATE 1      /* producers may overwrite the gathered buffer        */
+#define AGG_TR_PROD_DONE 2      /* this CTA's producers pushed all their parts        */
+#define AGG_TR_FIRST_WAIT 3     /* loader starts its first wait for a remote chunk    */
+#define AGG_TR_FIRST_READY 4    /* ... and sees it                                    */
+#define AGG_TR_LAST_READY 5     /* loader sees its last remote chunk                  */
+#define AGG_TR_FLAG_WAIT_NS 6   /* total time the loader waited on remote chunks      */
+#define AGG_TR_LOADER_DONE 7    /* loader issued its last k-block                     */
+#define AGG_TR_MMA_DONE 8       /* tensor-core issuer committed its last tile         */
+#define AGG_TR_EPI_DONE 9       /* epilogue stored its last tile                      */
+#define AGG_TR_END 10           /* CTA end                                            */
+#define AGG_TR_TILES 11         /* tiles this CTA processed (a count, not a time)     */
 
 /* ---- library ---------------------------------------------------------------------- */
 int agg_version(void);                 /* 100 * major + minor */

@@ -38,7 +38,7 @@ def test_abi_struct_sizes_match_python(pkg):
     a = ctypes.c_size_t()
     r = ctypes.c_size_t()
     assert pkg.lib().agg_abi_sizes(ctypes.byref(a), ctypes.byref(r)) == 0
-    assert a.value == ctypes.sizeof(pkg.agg.agg_args) == 200
+    assert a.value == ctypes.sizeof(pkg.agg.agg_args) == 208
     assert r.value == ctypes.sizeof(pkg.agg.agg_rank_info)
     assert pkg.lib().agg_version() == 100
 

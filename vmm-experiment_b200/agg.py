@@ -36,6 +36,31 @@ AGG_FLAG_CHUNK_OFF = 0
 AGG_FLAG_DONE_OFF = 32 << 10
 AGG_FLAG_USER_OFF = 36 << 10
 ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain"}
+AGG_TRACE_SLOTS = 16
+TRACE_EVENTS = ["start", "prod_gate", "prod_done", "first_wait", "first_ready", "last_ready", "flag_wait_ns",
+                "loader_done", "mma_done", "epi_done", "end", "tiles"]
+
+
+def trace_summary(rows):
+    """Summarise a [grid, AGG_TRACE_SLOTS] u64 trace (numpy) of one launch: for
+    each event, microseconds after the earliest CTA start (min / median / max
+    over the CTAs that recorded it); durations and counts as they are."""
+    import numpy as np
+
+    rows = np.asarray(rows, dtype=np.uint64)
+    t0 = rows[:, 0][rows[:, 0] > 0].min()
+    out = {}
+    for i, name in enumerate(TRACE_EVENTS):
+        col = rows[:, i]
+        col = col[col > 0]
+        if col.size == 0:
+            continue
+        if name in ("flag_wait_ns", "tiles"):
+            v = col.astype(np.float64) / (1e3 if name == "flag_wait_ns" else 1.0)
+        else:
+            v = (col - t0).astype(np.float64) / 1e3
+        out[name] = {"n": int(col.size), "min": float(v.min()), "med": float(np.median(v)), "max": float(v.max())}
+    return out
 
 # Every function the C ABI exports (include/agg.h).
 EXPORTS = [
@@ -92,6 +117,7 @@ class agg_args(ctypes.Structure):
         ("scale_b", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
+        ("trace", ctypes.c_void_p),
     ]
 
 
@@ -369,7 +395,12 @@ class AllGatherGemm:
         dt = torch.bfloat16 if self.elem == 2 else torch.uint8
         return device_view(self.slab.uc, (self.M, self.k), dt, self.device)
 
-    def __call__(self, A_r, B_r, out=None, scale_a=None, scale_b=None, stream=None):
+    def new_trace(self):
+        """A zeroed trace buffer for one launch (pass as `trace=`)."""
+        torch = _torch()
+        return torch.zeros((lib().agg_num_sms(), AGG_TRACE_SLOTS), dtype=torch.int64, device=self.device)
+
+    def __call__(self, A_r, B_r, out=None, scale_a=None, scale_b=None, stream=None, trace=None):
         torch = _torch()
         if A_r.shape != (self.m_local, self.k):
             raise AggError(f"A_r must be [{self.m_local}, {self.k}], got {tuple(A_r.shape)}")
@@ -392,6 +423,8 @@ class AllGatherGemm:
         a.dtype = AGG_DTYPE_E4M3 if self.elem == 1 else AGG_DTYPE_BF16
         a.status = self.status.data_ptr()
         a.timeout_ns = self.timeout_ns
+        if trace is not None:
+            a.trace = trace.data_ptr()
         if self.elem == 1:
             a.scale_a = scale_a.data_ptr()
             a.scale_b = scale_b.data_ptr()

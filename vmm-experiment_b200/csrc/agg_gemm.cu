@@ -99,6 +99,7 @@ struct alignas(64) KParams {
     const float* scale_b;
     void* c_ptr;  // C, for the epilogue that stores without TMA
     uint32_t* status;
+    unsigned long long* trace;  // optional per-CTA event times (AGG_TR_*)
     unsigned long long timeout_ns;
     uint32_t epoch;
     int rank, world;
@@ -134,6 +135,43 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& mt, in
     mt = m_tile_at(p, first + (j - nt * gs));
 }
 
+// ---- optional event trace (one row of AGG_TRACE_SLOTS u64 per CTA)
+__device__ __forceinline__ void trace_set(const KParams& p, int slot, unsigned long long v) {
+    if (p.trace) p.trace[blockIdx.x * AGG_TRACE_SLOTS + slot] = v;
+}
+__device__ __forceinline__ void trace_max(const KParams& p, int slot, unsigned long long v) {
+    if (p.trace) atomicMax(p.trace + blockIdx.x * AGG_TRACE_SLOTS + slot, v);
+}
+
+// Bookkeeping of a loader's waits on remote chunks.
+struct FlagWaitLog {
+    unsigned long long first_wait = 0, first_ready = 0, last_ready = 0, waited = 0;
+    int tiles = 0;
+    __device__ __forceinline__ bool wait(const KParams& p, const uint32_t* f, const Deadline& dl) {
+        const unsigned long long t0 = p.trace ? globaltimer_ns() : 0ull;
+        const bool ok = wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl);
+        if (p.trace) {
+            const unsigned long long t1 = globaltimer_ns();
+            if (!first_wait) {
+                first_wait = t0;
+                first_ready = t1;
+            }
+            last_ready = t1;
+            waited += t1 - t0;
+        }
+        return ok;
+    }
+    __device__ __forceinline__ void flush(const KParams& p) const {
+        if (!p.trace) return;
+        trace_set(p, AGG_TR_FIRST_WAIT, first_wait);
+        trace_set(p, AGG_TR_FIRST_READY, first_ready);
+        trace_set(p, AGG_TR_LAST_READY, last_ready);
+        trace_set(p, AGG_TR_FLAG_WAIT_NS, waited);
+        trace_set(p, AGG_TR_LOADER_DONE, globaltimer_ns());
+        trace_set(p, AGG_TR_TILES, static_cast<unsigned long long>(tiles));
+    }
+};
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
@@ -159,9 +197,11 @@ __device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uin
     uint32_t phase = 0;
     uint32_t used = 0, last_par = 0;
     bool ok = true;
+    FlagWaitLog log;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int mt, nt;
         tile_coords(p, t, mt, nt);
+        ++log.tiles;
         const CUtensorMap* tma = &p.tm_a_src;
         int a_row;
         if (p.world == 1) {
@@ -172,7 +212,7 @@ __device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uin
                 a_row = (mt - src * L) * BM;
             } else {
                 const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (mt - src * L);
-                if (!wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl)) {
+                if (!log.wait(p, f, dl)) {
                     record_failure(p.status, AGG_ROLE_FLAG, static_cast<uint32_t>(mt));
                     ok = false;
                     break;
@@ -204,6 +244,7 @@ __device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uin
             }
         }
     }
+    log.flush(p);
     // Never leave the CTA with TMA writes still landing in shared memory.
     for (int s = 0; s < STAGES; ++s)
         if (used & (1u << s))
@@ -265,6 +306,7 @@ __device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32
     // Every MMA this thread issued has finished once `drain` flips.
     umma_commit(drain);
     if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+    if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
 }
 
 __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base,
@@ -359,7 +401,10 @@ __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, u
             acc_phase ^= 1u;
         }
     }
-    if (lane == 0) bulk_wait_group<0>();
+    if (lane == 0) {
+        bulk_wait_group<0>();
+        if (p.trace) trace_max(p, AGG_TR_EPI_DONE, globaltimer_ns());
+    }
     __syncwarp();
 }
 
@@ -378,6 +423,7 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
         }
         fence_proxy_alias();
     }
+    if (p.trace && pw == 0 && lane == 0) trace_set(p, AGG_TR_PROD_GATE, globaltimer_ns());
     const int stride = static_cast<int>(gridDim.x) * PROD_WARPS;
     for (int q = static_cast<int>(blockIdx.x) * PROD_WARPS + pw; q < p.num_parts; q += stride) {
         const int c = q / p.ppc;
@@ -412,6 +458,7 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
         if (lane == 0) mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
         if (failed(p.status)) break;
     }
+    if (p.trace && lane == 0) trace_max(p, AGG_TR_PROD_DONE, globaltimer_ns());
 }
 
 // ---------------------------------------------------------------- kernel
@@ -432,6 +479,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
     Deadline dl;
     dl.end_ns = globaltimer_ns() + (p.timeout_ns ? p.timeout_ns : 10000000000ull);
     dl.status = p.status;
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_START, globaltimer_ns());
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -472,6 +520,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
     }
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_END, globaltimer_ns());
     if (p.world > 1 && threadIdx.x == 0) {
         // This CTA has finished reading gathered A for this launch.  The last CTA
         // on this GPU tells every GPU (release, system scope).
@@ -535,9 +584,11 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
     uint32_t phase = 0;
     uint32_t used = 0, last_par = 0;
     bool ok = true;
+    FlagWaitLog log;
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
         int mt, nt;
         tile_coords(p, t, mt, nt);
+        ++log.tiles;
         const int row = mt * G::TILE_M + static_cast<int>(crank) * 128;  // this CTA's first row of gathered A
         const CUtensorMap* tma = &p.tm_a_src;
         int a_row = row;
@@ -547,7 +598,7 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
                 a_row = row - src * p.m_local;
             } else {
                 const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (row - src * p.m_local) / BM;
-                if (!wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl)) {
+                if (!log.wait(p, f, dl)) {
                     record_failure(p.status, AGG_ROLE_FLAG, static_cast<uint32_t>(row / BM));
                     ok = false;
                     break;
@@ -578,6 +629,7 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
             }
         }
     }
+    log.flush(p);
     // The even CTA's `full` barriers count both CTAs' bytes of every phase it armed.
     if (crank == 0)
         for (int s = 0; s < G::STAGES; ++s)
@@ -641,6 +693,7 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     }
     umma_commit_pair_mc(drain, 0x1);
     if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+    if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
 }
 
 template <int BN2, int ST>
@@ -753,7 +806,10 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
             acc_phase ^= 1u;
         }
     }
-    if (lane == 0) bulk_wait_group<0>();
+    if (lane == 0) {
+        bulk_wait_group<0>();
+        if (p.trace) trace_max(p, AGG_TR_EPI_DONE, globaltimer_ns());
+    }
     __syncwarp();
 }
 
@@ -777,6 +833,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     Deadline dl;
     dl.end_ns = globaltimer_ns() + (p.timeout_ns ? p.timeout_ns : 10000000000ull);
     dl.status = p.status;
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_START, globaltimer_ns());
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < G::STAGES; ++s) {
@@ -826,6 +883,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, G::TMEM_COLS);
     }
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_END, globaltimer_ns());
     if (p.world > 1 && threadIdx.x == 0) {
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
@@ -1048,6 +1106,7 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.scale_b = a->scale_b;
     p.status = a->status;
     p.timeout_ns = a->timeout_ns;
+    p.trace = reinterpret_cast<unsigned long long*>(a->trace);
     p.epoch = a->A_copy_epoch;
 
     if (world > 1) {
