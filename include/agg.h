@@ -70,12 +70,20 @@ extern "C" {
 #define AGG_MAX_RANKS 8
 #define AGG_TILE_M 128                 /* rows per arrival chunk (= MMA tile height)     */
 #define AGG_MAX_CHUNKS 1024            /* per source rank: M/P <= 131072 rows            */
-#define AGG_PARTS_PER_CHUNK 64         /* arrivals per chunk per launch (flag target =   */
-                                       /* epoch * AGG_PARTS_PER_CHUNK)                   */
-#define AGG_FLAG_BYTES (64u << 10)     /* flag area zeroed at init                       */
-#define AGG_FLAG_CHUNK_OFF 0u          /* u32 [AGG_MAX_RANKS][AGG_MAX_CHUNKS] arrivals   */
-#define AGG_FLAG_DONE_OFF (32u << 10)  /* u32 end-of-launch counter                      */
-#define AGG_FLAG_USER_OFF (36u << 10)  /* free for mm_barrier rows / tests (28 KiB)      */
+#define AGG_FLAG_BYTES (128u << 10)    /* flag area, zeroed at init:                     */
+#define AGG_FLAG_CHUNK_OFF 0u          /* u32 [2][AGG_MAX_RANKS][AGG_MAX_CHUNKS] arrival */
+                                       /* counters, one set per launch parity; each     */
+                                       /* chunk's counter grows by one per launch       */
+#define AGG_FLAG_DONE_OFF (64u << 10)  /* u32 end-of-launch counter (one per rank and    */
+                                       /* launch); +64 B: this GPU's CTA counter;        */
+                                       /* +4 KiB: u32 [AGG_MAX_CHUNKS] producer counters */
+#define AGG_FLAG_USER_OFF (72u << 10)  /* free for mm_barrier rows / tests (56 KiB)      */
+
+/* agg_args.flags bits */
+#define AGG_ARGS_DOUBLE_BUFFER 1u      /* gathered A has two [M, K] regions used by     */
+                                       /* launch parity (A_local_buf / A_mc point at    */
+                                       /* region 0, region 1 follows), so a launch never */
+                                       /* waits for the other ranks' previous launch    */
 
 /* Per-rank view of the multicast slab (RankState of the reference, C layout). */
 typedef struct agg_rank_info {
@@ -106,7 +114,8 @@ typedef struct agg_args {
     const void* B;
     /* C_r [M, N_r] row-major bf16 output. */
     void* C;
-    /* Arrival flags, this GPU's unicast view (u32 [AGG_MAX_RANKS][AGG_MAX_CHUNKS]). */
+    /* Arrival counters, this GPU's unicast view of the flag area's chunk sets
+       (u32 [2][AGG_MAX_RANKS][AGG_MAX_CHUNKS], AGG_FLAG_CHUNK_OFF). */
     uint32_t* A_copy_ready;
     /* Launch epoch, >= 1, incremented by exactly one per launch on every rank. */
     uint32_t A_copy_epoch;
@@ -117,10 +126,10 @@ typedef struct agg_args {
     int32_t K;
     int32_t world;
     int32_t dtype;                 /* AGG_DTYPE_BF16 / AGG_DTYPE_E4M3 */
-    int32_t flags;                 /* reserved, 0 */
+    int32_t flags;                 /* AGG_ARGS_* bits */
     const void* A_src;             /* this rank's shard [M/world, K]; NULL = inside A_local_buf */
     uint32_t* A_copy_ready_mc;     /* multicast view of the flag array */
-    uint32_t* done_uc;             /* end-of-launch counter, unicast view */
+    uint32_t* done_uc;             /* end-of-launch counter, unicast view (AGG_FLAG_DONE_OFF) */
     uint32_t* done_mc;             /* end-of-launch counter, multicast view */
     const float* scale_a;          /* e4m3: per-row scale of gathered A [M] */
     const float* scale_b;          /* e4m3: per-row scale of B_r [N_r] (per output column) */

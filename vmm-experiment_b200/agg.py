@@ -30,11 +30,11 @@ AGG_DTYPE_E4M3 = 1
 AGG_MAX_RANKS = 8
 AGG_TILE_M = 128
 AGG_MAX_CHUNKS = 1024
-AGG_PARTS_PER_CHUNK = 64
-AGG_FLAG_BYTES = 64 << 10
+AGG_FLAG_BYTES = 128 << 10
 AGG_FLAG_CHUNK_OFF = 0
-AGG_FLAG_DONE_OFF = 32 << 10
-AGG_FLAG_USER_OFF = 36 << 10
+AGG_FLAG_DONE_OFF = 64 << 10
+AGG_FLAG_USER_OFF = 72 << 10
+AGG_ARGS_DOUBLE_BUFFER = 1
 ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain"}
 AGG_TRACE_SLOTS = 16
 TRACE_EVENTS = ["start", "prod_gate", "prod_done", "first_wait", "first_ready", "last_ready", "flag_wait_ns",
@@ -353,11 +353,13 @@ class AllGatherGemm:
 
     world == 1 (or no process group) runs the same kernel as a plain GEMM.
     The gathered activation lives in this GPU's multicast slab; the rank's own
-    shard is read from the caller's tensor.
+    shard is read from the caller's tensor.  With `double_buffer` (default) the
+    slab holds two gathered regions used by launch parity, so consecutive
+    launches never wait for each other across ranks.
     """
 
     def __init__(self, m_local: int, k: int, *, dtype: str = "bf16", group=None, device=None,
-                 timeout_s: float = 10.0, host_group=None):
+                 timeout_s: float = 10.0, host_group=None, double_buffer: bool = True):
         torch = _torch()
         import torch.distributed as dist
 
@@ -374,26 +376,30 @@ class AllGatherGemm:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.epoch = 0
         self.slab = None
+        self.double_buffer = double_buffer
         if self.world > 1:
             if m_local % AGG_TILE_M:
                 raise AggError(f"rows per rank ({m_local}) must be a multiple of {AGG_TILE_M}")
             hg = host_group if host_group is not None else dist.new_group(backend="gloo")
             self._host_group = hg
             job = make_job_id(hg)
-            self.slab = MulticastSlab(self.rank, self.world, self.device.index, self.world * m_local * k * self.elem,
-                                      job, _default_group_barrier(hg))
+            regions = 2 if double_buffer else 1
+            self.slab = MulticastSlab(self.rank, self.world, self.device.index,
+                                      regions * self.world * m_local * k * self.elem, job, _default_group_barrier(hg))
 
     @property
     def M(self) -> int:
         return self.world * self.m_local
 
     def gathered(self):
-        """The gathered activation [M, K] in this GPU's slab (valid after a launch completes)."""
+        """The gathered activation [M, K] of the latest launch in this GPU's slab
+        (valid once that launch has completed)."""
         torch = _torch()
         if self.slab is None:
             raise AggError("no slab at world == 1")
         dt = torch.bfloat16 if self.elem == 2 else torch.uint8
-        return device_view(self.slab.uc, (self.M, self.k), dt, self.device)
+        region = (self.epoch & 1) if self.double_buffer else 0
+        return device_view(self.slab.uc + region * self.M * self.k * self.elem, (self.M, self.k), dt, self.device)
 
     def new_trace(self):
         """A zeroed trace buffer for one launch (pass as `trace=`)."""
@@ -438,6 +444,8 @@ class AllGatherGemm:
             a.A_copy_ready_mc = s.flags(mc=True)
             a.done_uc = s.done()
             a.done_mc = s.done(mc=True)
+            if self.double_buffer:
+                a.flags |= AGG_ARGS_DOUBLE_BUFFER
         check(lib().agg_launch(ctypes.byref(a), _stream_ptr(stream)), "agg_launch")
         return out
 

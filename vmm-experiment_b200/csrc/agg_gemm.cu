@@ -89,12 +89,14 @@ struct alignas(64) KParams {
     uint4* a_mc;            // multicast VA of this rank's slot in gathered A
     unsigned long long shard_bytes;
     unsigned long long chunk_bytes;
-    unsigned long long part_bytes;
-    uint32_t* flags_uc;
+    uint32_t* flags_uc;     // this launch's parity set, [AGG_MAX_RANKS][AGG_MAX_CHUNKS]
     uint32_t* flags_mc;
     uint32_t* done_uc;
     uint32_t* done_mc;
-    uint32_t* cta_counter;
+    uint32_t* cta_counter;  // this GPU's count of CTAs done with the launch
+    uint32_t* chunk_cnt;    // this GPU's count of producer warps done with each chunk
+    uint32_t flag_target;   // a chunk has arrived when its counter reaches this
+    uint32_t gate_done;     // producers start once the done counter reaches this
     const float* scale_a;
     const float* scale_b;
     void* c_ptr;  // C, for the epilogue that stores without TMA
@@ -106,7 +108,7 @@ struct alignas(64) KParams {
     int M, N, K;
     int m_local;
     int num_m_tiles, num_n_tiles, num_tiles, num_kb;
-    int ppc, num_parts;
+    int num_chunks;
     int group_m;
     int dtype;
     int tile_m;  // rows per m-tile: 128 (one CTA) or 256 (a CTA pair)
@@ -149,7 +151,7 @@ struct FlagWaitLog {
     int tiles = 0;
     __device__ __forceinline__ bool wait(const KParams& p, const uint32_t* f, const Deadline& dl) {
         const unsigned long long t0 = p.trace ? globaltimer_ns() : 0ull;
-        const bool ok = wait_flag_geq(f, p.epoch * static_cast<uint32_t>(p.ppc), dl);
+        const bool ok = wait_flag_geq(f, p.flag_target, dl);
         if (p.trace) {
             const unsigned long long t1 = globaltimer_ns();
             if (!first_wait) {
@@ -411,11 +413,11 @@ __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, u
 __device__ __forceinline__ void role_producer(const KParams& p, int pw, const Deadline& dl) {
     const uint32_t lane = lane_id();
     int ok = 1;
-    if (p.epoch > 1) {
-        // Every rank must be done reading the previous launch's gathered A
-        // before this rank overwrites its slot on all GPUs.
-        if (lane == 0)
-            ok = wait_flag_geq(p.done_uc, (p.epoch - 1u) * static_cast<uint32_t>(p.world), dl) ? 1 : 0;
+    if (p.gate_done > 0) {
+        // Every rank must be done reading the gathered region this launch is
+        // about to overwrite (the previous launch, or the one before it when the
+        // region is double-buffered) before this rank writes its slot on all GPUs.
+        if (lane == 0) ok = wait_flag_geq(p.done_uc, p.gate_done, dl) ? 1 : 0;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_PROD, 0u);
@@ -424,15 +426,18 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
         fence_proxy_alias();
     }
     if (p.trace && pw == 0 && lane == 0) trace_set(p, AGG_TR_PROD_GATE, globaltimer_ns());
-    const int stride = static_cast<int>(gridDim.x) * PROD_WARPS;
-    for (int q = static_cast<int>(blockIdx.x) * PROD_WARPS + pw; q < p.num_parts; q += stride) {
-        const int c = q / p.ppc;
-        const int sub = q - c * p.ppc;
+    // Every producer warp of the grid takes one slice of chunk 0, then one of
+    // chunk 1, ...: the whole NVLink bandwidth goes to the earliest chunk, so
+    // chunks arrive one after another in the order the consumers need them.
+    const unsigned long long warps = static_cast<unsigned long long>(gridDim.x) * PROD_WARPS;
+    const unsigned long long w = static_cast<unsigned long long>(blockIdx.x) * PROD_WARPS + pw;
+    const unsigned long long slice = ((p.chunk_bytes + warps - 1) / warps + 15) / 16 * 16;
+    for (int c = 0; c < p.num_chunks; ++c) {
         const unsigned long long cbeg = static_cast<unsigned long long>(c) * p.chunk_bytes;
         unsigned long long cend = cbeg + p.chunk_bytes;
         if (cend > p.shard_bytes) cend = p.shard_bytes;
-        const unsigned long long beg = cbeg + static_cast<unsigned long long>(sub) * p.part_bytes;
-        unsigned long long end = beg + p.part_bytes;
+        const unsigned long long beg = cbeg + w * slice;
+        unsigned long long end = beg + slice;
         if (end > cend) end = cend;
         if (beg < end) {
             const uint4* s = p.a_src + beg / 16;
@@ -452,10 +457,19 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
                 }
             }
         }
-        // Order this warp's multicast stores before the flag, at system scope.
+        // This warp's slice is out: order its multicast stores (system scope)
+        // before its count; the warp that completes the count raises the
+        // chunk's arrival counter on every GPU, once per chunk and launch.
         fence_acq_rel_sys();
         __syncwarp();
-        if (lane == 0) mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
+        if (lane == 0) {
+            const uint32_t prev = atomicAdd(p.chunk_cnt + c, 1u);
+            if (prev == static_cast<uint32_t>(warps) - 1u) {
+                atomicExch(p.chunk_cnt + c, 0u);  // ready for the next launch
+                fence_acq_rel_sys();
+                mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
+            }
+        }
         if (failed(p.status)) break;
     }
     if (p.trace && lane == 0) trace_max(p, AGG_TR_PROD_DONE, globaltimer_ns());
@@ -1076,10 +1090,15 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     std::memset(&p, 0, sizeof(p));
     const CUtensorMapDataType dt = f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const uint32_t kb_elems = BK_BYTES / static_cast<uint32_t>(elem);
+    // Double buffering: launch e uses gathered region and flag set (e & 1).
+    const bool dbl = world > 1 && (a->flags & AGG_ARGS_DOUBLE_BUFFER) != 0;
+    const uint32_t parity = dbl ? (a->A_copy_epoch & 1u) : 0u;
+    const size_t region_off = static_cast<size_t>(parity) * a->M * a->K * elem;
     rc = encode_2d(&p.tm_a_src, dt, elem, a_src, a->K, world == 1 ? a->M : m_local, kb_elems, BM, "tensor map A shard");
     if (rc) return rc;
     if (world > 1) {
-        rc = encode_2d(&p.tm_a_gath, dt, elem, a->A_local_buf, a->K, a->M, kb_elems, BM, "tensor map gathered A");
+        rc = encode_2d(&p.tm_a_gath, dt, elem, static_cast<uint8_t*>(a->A_local_buf) + region_off, a->K, a->M,
+                       kb_elems, BM, "tensor map gathered A");
         if (rc) return rc;
     }
     rc = encode_2d(&p.tm_b, dt, elem, a->B, a->K, a->N, kb_elems, static_cast<uint32_t>(b_box), "tensor map B");
@@ -1110,25 +1129,26 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.epoch = a->A_copy_epoch;
 
     if (world > 1) {
-        p.a_mc = reinterpret_cast<uint4*>(a->A_mc + static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem);
+        p.a_mc = reinterpret_cast<uint4*>(a->A_mc + region_off +
+                                          static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem);
         p.shard_bytes = static_cast<unsigned long long>(m_local) * a->K * elem;
         p.chunk_bytes = static_cast<unsigned long long>(BM) * a->K * elem;
-        // Each chunk is pushed as AGG_PARTS_PER_CHUNK parts, handed to the producer
-        // warps round-robin in chunk order, so early chunks complete first.  The
-        // count is a constant of the protocol: a chunk's flag grows by exactly
-        // AGG_PARTS_PER_CHUNK per launch whatever the grid or shape.
-        const int chunks = m_local / BM;
-        const int ppc = AGG_PARTS_PER_CHUNK;
-        unsigned long long part = (p.chunk_bytes + ppc - 1) / ppc;
-        part = (part + 15) / 16 * 16;
-        p.part_bytes = part;
-        p.ppc = ppc;
-        p.num_parts = chunks * ppc;
-        p.flags_uc = a->A_copy_ready;
-        p.flags_mc = a->A_copy_ready_mc;
+        p.num_chunks = m_local / BM;
+        // Each chunk's counter grows by exactly one per launch (the last producer
+        // warp done with it raises it), so the target is the launch's ordinal
+        // within its flag set; the producer gate is the done count of the last
+        // launch that read the region being overwritten.
+        const uint32_t e = a->A_copy_epoch;
+        const uint32_t sets_per_rank = static_cast<uint32_t>(AGG_MAX_RANKS * AGG_MAX_CHUNKS);
+        p.flags_uc = a->A_copy_ready + parity * sets_per_rank;
+        p.flags_mc = a->A_copy_ready_mc + parity * sets_per_rank;
+        p.flag_target = dbl ? (e + 1u) >> 1 : e;
+        const uint32_t prior = dbl ? (e > 2u ? e - 2u : 0u) : e - 1u;
+        p.gate_done = prior * static_cast<uint32_t>(world);
         p.done_uc = a->done_uc;
         p.done_mc = a->done_mc;
-        p.cta_counter = a->done_uc + 16;
+        p.cta_counter = a->done_uc + 16;       // +64 B
+        p.chunk_cnt = a->done_uc + 1024;       // +4 KiB
         if (reinterpret_cast<uintptr_t>(a_src) % 16 || (p.a_mc && reinterpret_cast<uintptr_t>(p.a_mc) % 16))
             return fail(AGG_EINVAL, "agg_launch: shard pointers must be 16-byte aligned");
     }
