@@ -154,6 +154,10 @@ typedef struct agg_args {
 #define AGG_TR_EPI_DONE 9       /* epilogue stored its last tile                      */
 #define AGG_TR_END 10           /* CTA end                                            */
 #define AGG_TR_TILES 11         /* tiles this CTA processed (a count, not a time)     */
+#define AGG_TR_MMA_WAIT_NS 12   /* total time the MMA issuer waited for operand stages */
+#define AGG_TR_MMA_ACC_NS 13    /* ... and for a free accumulator                     */
+#define AGG_TR_LOAD_WAIT_NS 14  /* total time the loader waited for free stages       */
+#define AGG_TR_MMA_STALLS 15    /* operand-stage waits of the MMA issuer that blocked  */
 
 /* ---- library ---------------------------------------------------------------------- */
 int agg_version(void);                 /* 100 * major + minor */

@@ -58,7 +58,7 @@ def _bits_to_dev(bits, shape):
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16).reshape(shape)).view(torch.bfloat16).cuda()
 
 
-def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme):
+def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme, double_buffer=True):
     """Fused all-gather GEMM vs the oracle on the reference harness's inputs."""
     import numpy as np
     import torch
@@ -72,7 +72,7 @@ def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme):
         A_bits, A_ref, B_bits, B_ref = oracle.harness_inputs(world, m_local, k, n_r, scheme)
         A_r = _bits_to_dev(A_bits[rank], (m_local, k))
         B_r = _bits_to_dev(B_bits[rank], (n_r, k))
-        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
+        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD, double_buffer=double_buffer)
         outs = []
         for _ in range(launches):
             C = op(A_r, B_r)

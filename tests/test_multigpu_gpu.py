@@ -75,6 +75,14 @@ def test_smoke_workload_p2(scheme):
         assert r["launches_identical"], r
 
 
+def test_smoke_workload_p2_single_buffer():
+    """The single-region protocol (every launch waits for all ranks' previous one)."""
+    res = run_ranks("ag_gemm_parity", 2, m_local=512, k=1024, n_r=512, launches=4, scheme="reference",
+                    double_buffer=False)
+    for r in res:
+        assert r["gather_ok"] and r["bad"] == 0 and r["launches_identical"], r
+
+
 def test_reference_harness_shape_p2():
     """vmm/main.cpp:227-231 shapes scaled to two ranks: K=7168, N=6400, M_local=512."""
     res = run_ranks("ag_gemm_parity", 2, m_local=512, k=7168, n_r=6400, launches=1, scheme="reference")

@@ -38,7 +38,8 @@ AGG_ARGS_DOUBLE_BUFFER = 1
 ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain"}
 AGG_TRACE_SLOTS = 16
 TRACE_EVENTS = ["start", "prod_gate", "prod_done", "first_wait", "first_ready", "last_ready", "flag_wait_ns",
-                "loader_done", "mma_done", "epi_done", "end", "tiles"]
+                "loader_done", "mma_done", "epi_done", "end", "tiles", "mma_wait_ns", "mma_acc_ns", "load_wait_ns",
+                "mma_stalls"]
 
 
 def trace_summary(rows):
@@ -55,8 +56,8 @@ def trace_summary(rows):
         col = col[col > 0]
         if col.size == 0:
             continue
-        if name in ("flag_wait_ns", "tiles"):
-            v = col.astype(np.float64) / (1e3 if name == "flag_wait_ns" else 1.0)
+        if name.endswith("_ns") or name in ("tiles", "mma_stalls"):
+            v = col.astype(np.float64) / (1e3 if name.endswith("_ns") else 1.0)
         else:
             v = (col - t0).astype(np.float64) / 1e3
         out[name] = {"n": int(col.size), "min": float(v.min()), "med": float(np.median(v)), "max": float(v.max())}

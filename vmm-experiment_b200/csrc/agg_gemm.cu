@@ -94,7 +94,9 @@ struct alignas(64) KParams {
     uint32_t* done_uc;
     uint32_t* done_mc;
     uint32_t* cta_counter;  // this GPU's count of CTAs done with the launch
-    uint32_t* chunk_cnt;    // this GPU's count of producer warps done with each chunk
+    uint32_t* chunk_cnt;    // this GPU's count of pieces pushed, per chunk
+    unsigned long long* ticket;  // this GPU's next piece to push
+    unsigned long long piece_bytes;
     uint32_t flag_target;   // a chunk has arrived when its counter reaches this
     uint32_t gate_done;     // producers start once the done counter reaches this
     const float* scale_a;
@@ -145,9 +147,23 @@ __device__ __forceinline__ void trace_max(const KParams& p, int slot, unsigned l
     if (p.trace) atomicMax(p.trace + blockIdx.x * AGG_TRACE_SLOTS + slot, v);
 }
 
-// Bookkeeping of a loader's waits on remote chunks.
+// An mbarrier wait that, with tracing on, adds the time it blocked to `acc`
+// and counts the blocking waits in `n`.
+__device__ __forceinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity, const Deadline& dl, bool on,
+                                                unsigned long long& acc, unsigned long long& n) {
+    if (!on) return mbar_wait(bar, parity, dl);
+    if (mbar_try_wait(smem_u32(bar), parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    const bool ok = mbar_wait(bar, parity, dl);
+    acc += globaltimer_ns() - t0;
+    ++n;
+    return ok;
+}
+
+// Bookkeeping of a loader's waits on remote chunks and on free stages.
 struct FlagWaitLog {
     unsigned long long first_wait = 0, first_ready = 0, last_ready = 0, waited = 0;
+    unsigned long long stage_wait = 0, stage_waits = 0;
     int tiles = 0;
     __device__ __forceinline__ bool wait(const KParams& p, const uint32_t* f, const Deadline& dl) {
         const unsigned long long t0 = p.trace ? globaltimer_ns() : 0ull;
@@ -171,6 +187,7 @@ struct FlagWaitLog {
         trace_set(p, AGG_TR_FLAG_WAIT_NS, waited);
         trace_set(p, AGG_TR_LOADER_DONE, globaltimer_ns());
         trace_set(p, AGG_TR_TILES, static_cast<unsigned long long>(tiles));
+        trace_set(p, AGG_TR_LOAD_WAIT_NS, stage_wait);
     }
 };
 
@@ -228,7 +245,7 @@ __device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uin
             }
         }
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, dl)) {
+            if (!mbar_wait_timed(&empty[stage], phase ^ 1u, dl, p.trace != nullptr, log.stage_wait, log.stage_waits)) {
                 record_failure(p.status, AGG_ROLE_TMA, static_cast<uint32_t>(t));
                 ok = false;
                 break;
@@ -265,15 +282,16 @@ __device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
     for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, dl)) {
+        if (!mbar_wait_timed(&tempty[acc], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
             record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
             break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait(&full[stage], phase, dl)) {
+            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
                 record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
                 ok = false;
                 break;
@@ -308,7 +326,12 @@ __device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32
     // Every MMA this thread issued has finished once `drain` flips.
     umma_commit(drain);
     if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
-    if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    if (p.trace) {
+        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+        trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
+        trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
+        trace_set(p, AGG_TR_MMA_STALLS, full_waits);
+    }
 }
 
 __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base,
@@ -426,18 +449,25 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
         fence_proxy_alias();
     }
     if (p.trace && pw == 0 && lane == 0) trace_set(p, AGG_TR_PROD_GATE, globaltimer_ns());
-    // Every producer warp of the grid takes one slice of chunk 0, then one of
-    // chunk 1, ...: the whole NVLink bandwidth goes to the earliest chunk, so
-    // chunks arrive one after another in the order the consumers need them.
-    const unsigned long long warps = static_cast<unsigned long long>(gridDim.x) * PROD_WARPS;
-    const unsigned long long w = static_cast<unsigned long long>(blockIdx.x) * PROD_WARPS + pw;
-    const unsigned long long slice = ((p.chunk_bytes + warps - 1) / warps + 15) / 16 * 16;
-    for (int c = 0; c < p.num_chunks; ++c) {
+    // The shard is cut into pieces of `piece_bytes`, numbered in chunk order and
+    // handed out by a ticket counter, so the pieces in flight are always the
+    // earliest unfinished ones: chunks complete in the order the consumers need
+    // them.  The piece size (host-chosen) keeps enough bytes in flight to cover
+    // the NVLink round trip that each piece's system-scope fence waits for.
+    const unsigned long long pieces_per_chunk = (p.chunk_bytes + p.piece_bytes - 1) / p.piece_bytes;
+    const unsigned long long total = pieces_per_chunk * static_cast<unsigned long long>(p.num_chunks);
+    for (;;) {
+        unsigned long long ticket = 0;
+        if (lane == 0) ticket = atomicAdd(p.ticket, 1ull);
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket >= total) break;
+        const int c = static_cast<int>(ticket / pieces_per_chunk);
         const unsigned long long cbeg = static_cast<unsigned long long>(c) * p.chunk_bytes;
         unsigned long long cend = cbeg + p.chunk_bytes;
         if (cend > p.shard_bytes) cend = p.shard_bytes;
-        const unsigned long long beg = cbeg + w * slice;
-        unsigned long long end = beg + slice;
+        const unsigned long long beg = cbeg + (ticket - static_cast<unsigned long long>(c) * pieces_per_chunk) *
+                                                  p.piece_bytes;
+        unsigned long long end = beg + p.piece_bytes;
         if (end > cend) end = cend;
         if (beg < end) {
             const uint4* s = p.a_src + beg / 16;
@@ -457,14 +487,14 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
                 }
             }
         }
-        // This warp's slice is out: order its multicast stores (system scope)
+        // This warp's piece is out: order its multicast stores (system scope)
         // before its count; the warp that completes the count raises the
         // chunk's arrival counter on every GPU, once per chunk and launch.
         fence_acq_rel_sys();
         __syncwarp();
         if (lane == 0) {
             const uint32_t prev = atomicAdd(p.chunk_cnt + c, 1u);
-            if (prev == static_cast<uint32_t>(warps) - 1u) {
+            if (prev == static_cast<uint32_t>(pieces_per_chunk) - 1u) {
                 atomicExch(p.chunk_cnt + c, 0u);  // ready for the next launch
                 fence_acq_rel_sys();
                 mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
@@ -542,6 +572,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
             atomicExch(p.cta_counter, 0u);
+            atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
             mm_red_add_release_u32(p.done_mc, 1u);
         }
@@ -624,7 +655,7 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
         }
         const int b_row = nt * BN2 + static_cast<int>(crank) * G::B_ROWS;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, dl)) {
+            if (!mbar_wait_timed(&empty[stage], phase ^ 1u, dl, p.trace != nullptr, log.stage_wait, log.stage_waits)) {
                 record_failure(p.status, AGG_ROLE_TMA, static_cast<uint32_t>(t));
                 ok = false;
                 break;
@@ -666,15 +697,16 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, dl)) {
+        if (!mbar_wait_timed(&tempty[acc], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
             record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
             break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait(&full[stage], phase, dl)) {
+            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
                 record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
                 ok = false;
                 break;
@@ -707,7 +739,12 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     }
     umma_commit_pair_mc(drain, 0x1);
     if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
-    if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    if (p.trace) {
+        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+        trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
+        trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
+        trace_set(p, AGG_TR_MMA_STALLS, full_waits);
+    }
 }
 
 template <int BN2, int ST>
@@ -903,6 +940,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
             atomicExch(p.cta_counter, 0u);
+            atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
             mm_red_add_release_u32(p.done_mc, 1u);
         }
@@ -1147,8 +1185,23 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
         p.gate_done = prior * static_cast<uint32_t>(world);
         p.done_uc = a->done_uc;
         p.done_mc = a->done_mc;
-        p.cta_counter = a->done_uc + 16;       // +64 B
-        p.chunk_cnt = a->done_uc + 1024;       // +4 KiB
+        p.cta_counter = a->done_uc + 16;                                        // +64 B
+        p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);      // +128 B
+        p.chunk_cnt = a->done_uc + 1024;                                        // +4 KiB
+        // Piece size: the bytes in flight (producer warps x piece) should cover
+        // one system-scope round trip (~15 us) at this rank's share of the
+        // receivers' NVLink ingress (~600 GB/s, shared by world-1 senders), and
+        // never less than two chunks, so that chunks still complete in order.
+        const double egress = 600e9 / static_cast<double>(world - 1);
+        double window = egress * 15e-6;
+        window = std::max(window, 2.0 * static_cast<double>(p.chunk_bytes));
+        const int grid_ctas = pk ? 2 * std::max(1, std::min(pk->clusters, p.num_tiles))
+                                 : std::max(1, std::min(di->sms, p.num_tiles));
+        unsigned long long piece = static_cast<unsigned long long>(window / (grid_ctas * PROD_WARPS));
+        const int piece_env_kb = env_int("AGG_PIECE_KB", 0);
+        if (piece_env_kb > 0) piece = static_cast<unsigned long long>(piece_env_kb) << 10;
+        piece = std::min<unsigned long long>(std::max<unsigned long long>(piece, 4096ull), p.chunk_bytes);
+        p.piece_bytes = (piece + 511) / 512 * 512;
         if (reinterpret_cast<uintptr_t>(a_src) % 16 || (p.a_mc && reinterpret_cast<uintptr_t>(p.a_mc) % 16))
             return fail(AGG_EINVAL, "agg_launch: shard pointers must be 16-byte aligned");
     }
