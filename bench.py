@@ -172,9 +172,10 @@ def run_reference(args, rank, emit):
 METRIC = "all-gather GEMM TFLOP/s per GPU at 1/2/4/8 B200; % of roofline; vs NCCL+cuBLAS"
 
 
-def config_of(workload, world):
+def config_of(workload, world, dtype="bf16"):
     w = WORKLOADS[workload]
-    return {"workload": w["name"], "M": w["M"], "K": w["K"], "N_total": w["N"], "N_per_rank": w["N"] // world,
+    return {"workload": w["name"] + ("-e4m3" if dtype == "e4m3" else ""), "M": w["M"], "K": w["K"],
+            "N_total": w["N"], "N_per_rank": w["N"] // world,
             "M_per_rank": w["M"] // world, "P": world,
             "l2": "inputs larger than L2, no flush" if workload != "smoke" else "256 MiB L2 flush between steps",
             "parallelism": f"ag-tp{world}"}
@@ -214,6 +215,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mlp70b", choices=sorted(WORKLOADS))
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "e4m3"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-unfused", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -292,9 +294,21 @@ def main():
     B_r = (torch.randn(n_r, K, device=dev, generator=g) * 0.02).bfloat16()
     C_r = torch.empty(M, n_r, device=dev, dtype=torch.bfloat16)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if args.workload == "smoke" else None
+    f8 = args.dtype == "e4m3"
+    if f8:
+        # per-row amax e4m3 of A_r, per-output-column (= per row of B_r [N_r, K]) e4m3 of B_r
+        A_in, S_a = pkg.agg.quantize_rows_e4m3(A_r)
+        B_in, S_b = pkg.agg.quantize_rows_e4m3(B_r)
+        del A_r, B_r
+    else:
+        A_in, B_in, S_a, S_b = A_r, B_r, None, None
+    elem = 1 if f8 else 2
 
-    op = pkg.AllGatherGemm(m_local, K, host_group=host_group) if world > 1 else pkg.AllGatherGemm(m_local, K)
+    op = pkg.AllGatherGemm(m_local, K, dtype=args.dtype, host_group=host_group)
     stream = torch.cuda.current_stream()
+
+    def launch(A, out, trace=None):
+        return op(A, B_in, out=out, scale_a=S_a, scale_b=S_b, trace=trace)
 
     def barrier():
         if world > 1:
@@ -324,7 +338,7 @@ def main():
     def step_ours():
         if flush is not None:
             flush.fill_(1)
-        op(A_r, B_r, out=C_r)
+        launch(A_in, C_r)
 
     for _ in range(args.warmup):
         step_ours()
@@ -337,61 +351,75 @@ def main():
     clk = clocks.stop()
     op.check_status()
     # kernel-only time of the same launches (the flush is excluded for smoke)
-    kernel_ms = ms if flush is None else timed(lambda: op(A_r, B_r, out=C_r), args.steps)
+    kernel_ms = ms if flush is None else timed(lambda: launch(A_in, C_r), args.steps)
 
     flops_step = 2.0 * M * K * Ntot
     value = flops_step / (ms * 1e-3) / 1e12
     peaks = load_peaks()
     flops_rank = 2.0 * M * K * n_r
     achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
-    t_tc = flops_rank / (peaks["bf16"] * 1e12)
-    nvl_bytes = (world - 1) / world * M * K * 2 if world > 1 else 0.0
+    # e4m3 peak: twice the measured bf16 figure (the dense fp8 rate is twice bf16's)
+    peak_tc = peaks["bf16"] * (2.0 if f8 else 1.0)
+    t_tc = flops_rank / (peak_tc * 1e12)
+    nvl_bytes = (world - 1) / world * M * K * elem if world > 1 else 0.0
     t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
     t_roof = max(t_tc, t_nvl)
     traffic = ncu_traffic(args.workload)
-    roofline = {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "achieved": achieved, "peak": peaks["bf16"],
+    roofline = {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "achieved": achieved, "peak": peak_tc,
                 "unit": "TFLOP/s", "frac": t_roof / (kernel_ms * 1e-3),
-                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
+                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)" + (" x 2 for e4m3" if f8 else ""),
                 "traffic": traffic, "t_roof_ms": t_roof * 1e3, "t_tensor_ms": t_tc * 1e3, "t_nvlink_ms": t_nvl * 1e3,
-                "nvlink_bytes_per_rank": nvl_bytes}
+                "nvlink_bytes_per_rank": nvl_bytes, "nvlink_gbs": NVLINK_GBS}
 
     out = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (A~N(0,1), B~N(0,0.02), seeded per rank)",
-           "config": config_of(args.workload, world), "tflops_per_gpu": value / world,
+           "vs_baseline": None, "dtype": args.dtype,
+           "data": "synthetic (A~N(0,1), B~N(0,0.02), seeded per rank)" + (", per-row amax e4m3" if f8 else ""),
+           "config": config_of(args.workload, world, args.dtype), "tflops_per_gpu": value / world,
            "gpu_launches": args.steps, "roofline": roofline, "clocks": clk}
 
-    # ---- unfused baseline: NCCL all-gather + cuBLAS GEMM
+    # ---- unfused baseline: NCCL all-gather + cuBLAS GEMM (cuBLASLt fp8 for e4m3)
     if not args.no_unfused:
-        A_full = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+        A_full = torch.empty(M, K, device=dev, dtype=A_in.dtype)
+        S_full = torch.empty(M, device=dev, dtype=torch.float32) if f8 else None
         C_u = torch.empty(M, n_r, device=dev, dtype=torch.bfloat16)
 
         def step_unfused():
             if flush is not None:
                 flush.fill_(1)
             if world > 1:
-                dist.all_gather_into_tensor(A_full, A_r)
-                torch.matmul(A_full, B_r.t(), out=C_u)
+                dist.all_gather_into_tensor(A_full, A_in)
+                if f8:
+                    dist.all_gather_into_tensor(S_full, S_a)
+                a, sa = A_full, S_full
             else:
-                torch.matmul(A_r, B_r.t(), out=C_u)
+                a, sa = A_in, S_a
+            if f8:
+                C_u.copy_(torch._scaled_mm(a.view(torch.float8_e4m3fn), B_in.view(torch.float8_e4m3fn).t(),
+                                           scale_a=sa[:, None], scale_b=S_b[None, :], out_dtype=torch.bfloat16))
+            else:
+                torch.matmul(a, B_in.t(), out=C_u)
 
-        for _ in range(args.warmup):
-            step_unfused()
-        ums = timed(step_unfused, args.steps)
-        out["unfused_nccl_cublas"] = {"value": flops_step / (ums * 1e-3) / 1e12, "unit": "TFLOP/s",
-                                      "ms_per_step": ums, "speedup_fused": ums / ms}
+        try:
+            for _ in range(args.warmup):
+                step_unfused()
+            ums = timed(step_unfused, args.steps)
+            out["unfused_nccl_cublas"] = {"value": flops_step / (ums * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                          "ms_per_step": ums, "speedup_fused": ums / ms}
+        except RuntimeError as e:  # e.g. no rowwise-scaled fp8 GEMM in this torch build
+            out["unfused_nccl_cublas"] = {"unavailable": str(e).splitlines()[0][:200]}
         del A_full, C_u
 
     # ---- end to end through the public API with host buffers
     if not args.no_e2e:
-        A_host = torch.empty(m_local, K, dtype=torch.bfloat16, pin_memory=True)
-        A_host.copy_(A_r)
+        A_host = torch.empty(m_local, K, dtype=A_in.dtype, pin_memory=True)
+        A_host.copy_(A_in)
         C_host = torch.empty(M, n_r, dtype=torch.bfloat16, pin_memory=True)
-        A_dev = torch.empty_like(A_r)
+        A_dev = torch.empty_like(A_in)
 
         def step_e2e():
             A_dev.copy_(A_host, non_blocking=True)
-            op(A_dev, B_r, out=C_r)
+            launch(A_dev, C_r)
             C_host.copy_(C_r, non_blocking=True)
 
         for _ in range(max(1, args.warmup // 2)):
@@ -399,9 +427,8 @@ def main():
         e2e_steps = max(2, min(args.steps, 5))
         ems = timed(step_e2e, e2e_steps)
         out["e2e"] = {"value": flops_step / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
-                      "h2d_bytes_per_step": A_host.numel() * 2, "d2h_bytes_per_step": C_host.numel() * 2,
-                      "ms_per_step": ems, "steps": e2e_steps}
-        out["e2e"]["gpu_launches"] = e2e_steps
+                      "h2d_bytes_per_step": A_host.numel() * elem, "d2h_bytes_per_step": C_host.numel() * 2,
+                      "ms_per_step": ems, "steps": e2e_steps, "gpu_launches": e2e_steps}
         op.check_status()
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -412,7 +439,7 @@ def main():
         tr = op.new_trace()
         torch.cuda.synchronize()
         barrier()
-        op(A_r, B_r, out=C_r, trace=tr)
+        launch(A_in, C_r, trace=tr)
         torch.cuda.synchronize()
         op.check_status()
         rows = tr.cpu().numpy()
@@ -422,7 +449,7 @@ def main():
             dist.all_gather_object(per_rank, rows, group=host_group)
         if rank == 0:
             with open(args.trace, "w") as f:
-                json.dump({"workload": config_of(args.workload, world),
+                json.dump({"workload": config_of(args.workload, world, args.dtype),
                            "ranks": [pkg.agg.trace_summary(r) for r in per_rank]}, f, indent=1)
 
     op.close()

@@ -131,7 +131,10 @@ typedef struct agg_args {
     uint32_t* A_copy_ready_mc;     /* multicast view of the flag array */
     uint32_t* done_uc;             /* end-of-launch counter, unicast view (AGG_FLAG_DONE_OFF) */
     uint32_t* done_mc;             /* end-of-launch counter, multicast view */
-    const float* scale_a;          /* e4m3: per-row scale of gathered A [M] */
+    const float* scale_a;          /* e4m3: per-row scales of A_src, 16-byte aligned: [M] at
+                                      world 1, this rank's [M/world] otherwise (the kernel
+                                      gathers them into the slab right after the gathered
+                                      A region(s): float [M] per region) */
     const float* scale_b;          /* e4m3: per-row scale of B_r [N_r] (per output column) */
     uint32_t* status;              /* device status word (AGG_STATUS_*), may be NULL */
     uint64_t timeout_ns;           /* bound on every device-side wait; 0 = 10 s */

@@ -219,8 +219,18 @@ def e4m3_table() -> np.ndarray:
 
 def quantize_e4m3_rows(x: np.ndarray):
     """Per-row amax scaling: s = amax/448, q = e4m3(x / s).  Returns (q uint8, s float32[rows])."""
-    x = np.asarray(x, dtype=np.float32)
-    amax = np.max(np.abs(x), axis=1)
-    s = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
-    q = f32_to_e4m3(x / s[:, None])
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), dtype=np.uint8)
+    s = np.empty(rows, dtype=np.float32)
+    L = lib()
+    L.orc_quantize_e4m3_rows.argtypes = [_f32p, ctypes.c_long, ctypes.c_long,
+                                         ctypes.POINTER(ctypes.c_uint8), _f32p]
+    L.orc_quantize_e4m3_rows(_p(x, _f32p), rows, cols, q.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                             _p(s, _f32p))
     return q, s
+
+
+def dequantize_e4m3_rows(q: np.ndarray, s: np.ndarray) -> np.ndarray:
+    """q * s per row, exactly (every e4m3 value times an fp32 scale is an fp32 product)."""
+    return e4m3_table()[np.asarray(q, dtype=np.uint8)] * np.asarray(s, np.float32)[:, None]

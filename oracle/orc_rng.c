@@ -160,6 +160,22 @@ uint8_t orc_f32_to_e4m3(float f) {
     return (uint8_t)(sign | (uint8_t)(ef << 3) | (uint8_t)(m - 8u));
 }
 
+/* Per-row amax quantization (the fp8 workload's recipe): s[r] = amax_r / 448
+   (1 for an all-zero row), q[r][c] = e4m3(x[r][c] / s[r]). */
+void orc_quantize_e4m3_rows(const float* x, long rows, long cols, uint8_t* q, float* s) {
+    for (long r = 0; r < rows; ++r) {
+        const float* xr = x + r * cols;
+        float amax = 0.0f;
+        for (long c = 0; c < cols; ++c) {
+            const float a = fabsf(xr[c]);
+            if (a > amax) amax = a;
+        }
+        const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
+        s[r] = sc;
+        for (long c = 0; c < cols; ++c) q[r * cols + c] = orc_f32_to_e4m3(xr[c] / sc);
+    }
+}
+
 float orc_e4m3_to_f32(uint8_t q) {
     const int sign = q & 0x80;
     const int ef = (q >> 3) & 0xf;

@@ -95,6 +95,46 @@ def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme, double_
         _teardown(op)
 
 
+def ag_gemm_e4m3_parity(rank, world, port, m_local, k, n_r, launches):
+    """e4m3 fused all-gather GEMM (scales gathered with the chunks) vs the oracle."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+
+    pkg = _init(rank, world, port)
+    op = None
+    try:
+        shards = []
+        for s in range(world):
+            x = np.random.default_rng(11 + s).standard_normal((m_local, k)).astype(np.float32)
+            shards.append(oracle.quantize_e4m3_rows(x))
+        wb = (np.random.default_rng(99 + rank).standard_normal((n_r, k)) * 0.02).astype(np.float32)
+        qb, sb = oracle.quantize_e4m3_rows(wb)
+        dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+        qa, sa = shards[rank]
+        op = pkg.AllGatherGemm(m_local, k, dtype="e4m3", host_group=dist.group.WORLD)
+        A_r, S_a, B_r, S_b = dev(qa), dev(sa), dev(qb), dev(sb)
+        outs = []
+        for _ in range(launches):
+            outs.append(op(A_r, B_r, scale_a=S_a, scale_b=S_b))
+        torch.cuda.synchronize()
+        op.check_status()
+        full = np.concatenate([oracle.dequantize_e4m3_rows(q, s) for q, s in shards])
+        want = oracle.gemm_f64(full, oracle.dequantize_e4m3_rows(qb, sb)).astype(np.float32)
+        got = outs[-1].float().cpu().numpy()
+        stats = oracle.error_stats(got, want)
+        bad, where = oracle.check_close(got, want)
+        gathered = op.gathered().cpu().numpy()
+        gather_ok = bool(np.array_equal(gathered, np.concatenate([q for q, _ in shards])))
+        same = all(torch.equal(o, outs[0]) for o in outs)
+        return {"rank": rank, "stats": stats, "bad": bad, "where": where, "gather_ok": gather_ok,
+                "launches_identical": same}
+    finally:
+        _teardown(op)
+
+
 def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches):
     """Back-to-back launches with different activations: each output must match
     its own inputs (checks the end-of-launch barrier that guards the gathered

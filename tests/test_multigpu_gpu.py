@@ -90,6 +90,14 @@ def test_reference_harness_shape_p2():
         assert r["gather_ok"] and r["bad"] == 0 and r["stats"]["max_rel_err"] <= 1e-2, r
 
 
+def test_e4m3_fused_p2():
+    """e4m3 A/B with per-row scales; the remote rows' scales travel with their chunks."""
+    res = run_ranks("ag_gemm_e4m3_parity", 2, m_local=512, k=1024, n_r=768, launches=3)
+    for r in res:
+        assert r["gather_ok"] and r["bad"] == 0 and r["launches_identical"], r
+        assert r["stats"]["max_rel_err"] <= 3e-2, r
+
+
 def test_back_to_back_launches_with_new_inputs_p2():
     res = run_ranks("ag_gemm_changing_inputs", 2, m_local=1024, k=2048, n_r=1024, launches=6)
     for r in res:

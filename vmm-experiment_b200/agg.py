@@ -252,6 +252,17 @@ def gemm(A, B, out=None, status=None, stream=None):
     return out
 
 
+def quantize_rows_e4m3(x):
+    """Per-row amax scaling to e4m3 on the device: s = amax/448 (1 for an all-zero
+    row), q = e4m3(x / s) rounded to nearest even.  Returns (uint8 payload, float32 s)."""
+    torch = _torch()
+    xf = x.float()
+    amax = xf.abs().amax(dim=1)
+    s = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax)).contiguous()
+    q = (xf / s[:, None]).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
+    return q, s
+
+
 def gemm_e4m3(A_q, B_q, scale_a, scale_b, out=None, status=None, stream=None):
     """C = (s_a[:,None] * A_q) . (s_b[:,None] * B_q)^T with e4m3 operands (uint8 payloads)."""
     torch = _torch()
@@ -385,8 +396,10 @@ class AllGatherGemm:
             self._host_group = hg
             job = make_job_id(hg)
             regions = 2 if double_buffer else 1
-            self.slab = MulticastSlab(self.rank, self.world, self.device.index,
-                                      regions * self.world * m_local * k * self.elem, job, _default_group_barrier(hg))
+            M = self.world * m_local
+            data = regions * M * k * self.elem + (regions * M * 4 if self.elem == 1 else 0)  # + gathered scales
+            self.slab = MulticastSlab(self.rank, self.world, self.device.index, data, job,
+                                      _default_group_barrier(hg))
 
     @property
     def M(self) -> int:

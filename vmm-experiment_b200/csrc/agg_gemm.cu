@@ -99,8 +99,10 @@ struct alignas(64) KParams {
     unsigned long long piece_bytes;
     uint32_t flag_target;   // a chunk has arrived when its counter reaches this
     uint32_t gate_done;     // producers start once the done counter reaches this
-    const float* scale_a;
-    const float* scale_b;
+    const float* scale_a;     // e4m3: row scales of A_src ([M] at world 1, the shard's [M/world] otherwise)
+    const float* scale_b;     // e4m3: row scales of B ([N])
+    const float* scale_gath;  // e4m3, world > 1: gathered row scales [M] (this GPU's view)
+    float* scale_mc;          // e4m3, world > 1: this rank's slot of them, multicast view
     void* c_ptr;  // C, for the epilogue that stores without TMA
     uint32_t* status;
     unsigned long long* trace;  // optional per-CTA event times (AGG_TR_*)
@@ -190,6 +192,26 @@ struct FlagWaitLog {
         trace_set(p, AGG_TR_LOAD_WAIT_NS, stage_wait);
     }
 };
+
+// e4m3 epilogue: the scale of row (row0 + lane).  A remote shard's scales came
+// with its chunk (see the producer); the warp's 32 rows lie in one chunk, whose
+// arrival lane 0 re-acquires before the lanes read the gathered scales.
+__device__ __forceinline__ float epilogue_row_scale(const KParams& p, int row0, uint32_t lane, const Deadline& dl) {
+    const int row = row0 + static_cast<int>(lane);
+    if (p.world == 1) return row < p.M ? __ldg(p.scale_a + row) : 0.0f;
+    const int src = row0 / p.m_local;
+    if (src == p.rank) return __ldg(p.scale_a + (row - src * p.m_local));
+    int ok = 1;
+    if (lane == 0) {
+        const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (row0 - src * p.m_local) / BM;
+        ok = wait_flag_geq(f, p.flag_target, dl) ? 1 : 0;
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) return 0.0f;
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p.scale_gath + row) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -358,11 +380,7 @@ __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, u
         const uint32_t tbase =
             tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + static_cast<uint32_t>(acc * BN);
         const int row0 = mt * BM + eg * 32;
-        float row_scale = 1.0f;
-        if (f8) {
-            const int row = row0 + static_cast<int>(lane);
-            row_scale = row < p.M ? __ldg(p.scale_a + row) : 0.0f;
-        }
+        const float row_scale = f8 ? epilogue_row_scale(p, row0, lane, dl) : 1.0f;
 #pragma unroll 1
         for (int j = 0; j < BN / EPI_COLS; ++j) {
             uint32_t r0[32], r1[32];
@@ -485,6 +503,17 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
                     const unsigned long long j = i + 32ull * u;
                     if (j < n) mm_st_v4(d + j, v[u]);
                 }
+            }
+        }
+        if (p.scale_mc && ticket == static_cast<unsigned long long>(c) * pieces_per_chunk) {
+            // e4m3: the first piece of a chunk also carries the chunk's 128 row
+            // scales (512 bytes, one 16-byte store per lane), so the chunk's
+            // arrival counter covers them too.
+            const int row = c * BM + static_cast<int>(lane) * 4;
+            if (row < p.m_local) {
+                const float4 sv = *reinterpret_cast<const float4*>(p.scale_a + row);
+                mm_st_v4(p.scale_mc + row, make_uint4(__float_as_uint(sv.x), __float_as_uint(sv.y),
+                                                      __float_as_uint(sv.z), __float_as_uint(sv.w)));
             }
         }
         // This warp's piece is out: order its multicast stores (system scope)
@@ -774,11 +803,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
         const uint32_t tbase =
             tmem_base + (static_cast<uint32_t>(eg * 32) << 16) + static_cast<uint32_t>(acc * BN2);
         const int row0 = mt * G::TILE_M + static_cast<int>(crank) * 128 + eg * 32;
-        float row_scale = 1.0f;
-        if (f8) {
-            const int row = row0 + static_cast<int>(lane);
-            row_scale = row < p.M ? __ldg(p.scale_a + row) : 0.0f;
-        }
+        const float row_scale = f8 ? epilogue_row_scale(p, row0, lane, dl) : 1.0f;
 #pragma unroll 1
         for (int j = 0; j < BN2 / EPI_COLS; ++j) {
             uint32_t r0[32], r1[32];
@@ -1188,6 +1213,15 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
         p.cta_counter = a->done_uc + 16;                                        // +64 B
         p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);      // +128 B
         p.chunk_cnt = a->done_uc + 1024;                                        // +4 KiB
+        if (f8) {
+            // Gathered row scales follow the gathered region(s): float [M] per parity.
+            const size_t scales_off = static_cast<size_t>(dbl ? 2 : 1) * a->M * a->K * elem +
+                                      static_cast<size_t>(parity) * a->M * sizeof(float);
+            p.scale_gath = reinterpret_cast<const float*>(static_cast<uint8_t*>(a->A_local_buf) + scales_off);
+            p.scale_mc = reinterpret_cast<float*>(a->A_mc + scales_off) + static_cast<size_t>(a->dev_idx) * m_local;
+            if (reinterpret_cast<uintptr_t>(a->scale_a) % 16)
+                return fail(AGG_EINVAL, "agg_launch: scale_a must be 16-byte aligned");
+        }
         // Piece size: the bytes in flight (producer warps x piece) should cover
         // one system-scope round trip (~15 us) at this rank's share of the
         // receivers' NVLink ingress (~600 GB/s, shared by world-1 senders), and
