@@ -258,7 +258,9 @@ def quantize_rows_e4m3(x):
     torch = _torch()
     xf = x.float()
     amax = xf.abs().amax(dim=1)
-    s = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax)).contiguous()
+    # tensor / tensor is an IEEE division (a Python scalar divisor becomes a
+    # multiplication by its rounded reciprocal)
+    s = torch.where(amax > 0, amax / torch.full_like(amax, 448.0), torch.ones_like(amax)).contiguous()
     q = (xf / s[:, None]).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8).contiguous()
     return q, s
 
