@@ -8,16 +8,16 @@ after scaling, and the reference's check_close on every element.
 import numpy as np
 import pytest
 
-from test_gemm_gpu import VARIANTS  # noqa: F401  (same kernel variants)
+from test_gemm_gpu import ENV_KNOBS, VARIANTS  # same kernel variants
 
 pytestmark = pytest.mark.gpu
 
 MAX_REL_F8 = 3e-2
 
 
-@pytest.fixture(params=["1sm", "pair256", "pair128"])
+@pytest.fixture(params=["1sm", "pair256", "pair128", "pair256k1"])
 def f8_variant(request, monkeypatch):
-    for k in ("AGG_KERNEL", "AGG_BN", "AGG_STAGES"):
+    for k in ENV_KNOBS:
         monkeypatch.delenv(k, raising=False)
     for k, v in VARIANTS[request.param].items():
         monkeypatch.setenv(k, v)

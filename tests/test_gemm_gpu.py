@@ -17,15 +17,16 @@ MAX_REL = 1e-2
 # Kernel variants selectable at launch time: the one-CTA kernel (128 x 256 tiles)
 # and the CTA-pair kernel (256 x 256 or 256 x 128 tiles).
 VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
-            "pair256": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_STAGES": "6"},
-            "pair256s7": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_STAGES": "7"},
-            "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_STAGES": "8"},
-            "pair128s9": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_STAGES": "9"}}
+            "pair256": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "2"},
+            "pair256k1": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "1"},
+            "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "2"},
+            "pair128k1": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "1"}}
+ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB")
 
 
 @pytest.fixture(params=sorted(VARIANTS))
 def variant(request, monkeypatch):
-    for k in ("AGG_KERNEL", "AGG_BN", "AGG_STAGES"):
+    for k in ENV_KNOBS:
         monkeypatch.delenv(k, raising=False)
     for k, v in VARIANTS[request.param].items():
         monkeypatch.setenv(k, v)

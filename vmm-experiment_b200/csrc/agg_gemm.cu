@@ -318,7 +318,8 @@ __device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32
                 ok = false;
                 break;
             }
-            tc_fence_after();
+            // (No tcgen05 fence here: the stage was filled by TMA and the mbarrier
+            // wait already orders those async-proxy writes before the MMA reads.)
             const uint32_t sa = smem_u32(smem + SMEM_STAGE_OFF + stage * STAGE_BYTES);
             const uint64_t adesc = sw128_kmajor_desc(sa);
             const uint64_t bdesc = sw128_kmajor_desc(sa + A_STAGE_BYTES);
@@ -614,7 +615,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
 // per k-step: the pair computes a 256 x BN tile, each CTA holding 128 rows of A
 // and BN/2 rows of B in its shared memory and 128 x BN accumulators in its TMEM.
 // Per SM that halves the B traffic from L2 and the smem bytes the tensor core
-// reads per FLOP, and frees room for 6 (BN=256) or 8 (BN=128) pipeline stages.
+// reads per FLOP.  A stage holds SUB 128-byte-wide k sub-blocks (one TMA box
+// per operand and sub-block): with SUB = 2 the issuer runs 8 MMAs per barrier
+// round trip, which is what keeps the tensor pipe busy; 3 (BN=256) or 4
+// (BN=128) such stages fill the shared memory.
 //
 //   both CTAs   loader: waits on its own `empty` barrier, TMA-loads its A half
 //               and B half, completion counted on the EVEN CTA's `full` barrier
@@ -622,12 +626,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
 //   even CTA    MMA issuer: waits `full`, issues the pair MMA, commits to
 //               `empty` in both CTAs, and to `tfull` in both CTAs per tile;
 //   both CTAs   epilogue: drains its own TMEM, arrives on the even CTA's `tempty`.
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 struct PairCfg {
     static constexpr int TILE_M = 256;
     static constexpr int B_ROWS = BN2 / 2;
-    static constexpr int A_BYTES = 128 * BK_BYTES;
-    static constexpr int B_BYTES = B_ROWS * BK_BYTES;
+    static constexpr int A_SUB = 128 * BK_BYTES;     // one k sub-block of A (16 KiB)
+    static constexpr int B_SUB = B_ROWS * BK_BYTES;  // one k sub-block of B
+    static constexpr int A_BYTES = SUB * A_SUB;
+    static constexpr int B_BYTES = SUB * B_SUB;
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int STAGES = ST;
     static constexpr int EPI_OFF = STAGES * STAGE;
@@ -644,10 +650,10 @@ struct PairCfg {
     static_assert(STAGES <= 32, "stage masks are 32-bit");
 };
 
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             uint32_t crank, const Deadline& dl) {
-    using G = PairCfg<BN2, ST>;
+    using G = PairCfg<BN2, ST, SUB>;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
     if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
@@ -693,8 +699,12 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
             uint8_t* sb = sa + G::A_BYTES;
             if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE);
             const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_2d_pair(tma, sa, bar, kb * kb_elems, a_row);
-            tma_load_2d_pair(&p.tm_b, sb, bar, kb * kb_elems, b_row);
+#pragma unroll
+            for (int u = 0; u < SUB; ++u) {
+                const int kx = (kb * SUB + u) * kb_elems;
+                tma_load_2d_pair(tma, sa + u * G::A_SUB, bar, kx, a_row);
+                tma_load_2d_pair(&p.tm_b, sb + u * G::B_SUB, bar, kx, b_row);
+            }
             used |= 1u << stage;
             last_par = (last_par & ~(1u << stage)) | (phase << stage);
             if (++stage == G::STAGES) {
@@ -712,11 +722,11 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
                     record_failure(p.status, AGG_ROLE_DRAIN, 1u);
 }
 
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
                                          uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
                                          const Deadline& dl) {
-    using G = PairCfg<BN2, ST>;
+    using G = PairCfg<BN2, ST, SUB>;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
     const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, BN2) : make_idesc(1, 1, G::TILE_M, BN2);
     const int cluster_id = static_cast<int>(blockIdx.x >> 1);
@@ -740,18 +750,21 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
                 ok = false;
                 break;
             }
-            tc_fence_after();
+            // (No tcgen05 fence here: TMA filled the stage, the mbarrier orders it.)
             const uint32_t sa = smem_u32(smem + stage * G::STAGE);
-            const uint64_t adesc = sw128_kmajor_desc(sa);
-            const uint64_t bdesc = sw128_kmajor_desc(sa + G::A_BYTES);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t off = static_cast<uint64_t>(k * 2);
-                const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
-                if (f8)
-                    umma_f8_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
-                else
-                    umma_f16_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+            for (int u = 0; u < SUB; ++u) {
+                const uint64_t adesc = sw128_kmajor_desc(sa + u * G::A_SUB);
+                const uint64_t bdesc = sw128_kmajor_desc(sa + G::A_BYTES + u * G::B_SUB);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint64_t off = static_cast<uint64_t>(k * 2);
+                    const uint32_t accumulate = (kb > 0 || u > 0 || k > 0) ? 1u : 0u;
+                    if (f8)
+                        umma_f8_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                    else
+                        umma_f16_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                }
             }
             umma_commit_pair_mc(&empty[stage], 0x3);
             if (++stage == G::STAGES) {
@@ -776,10 +789,10 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     }
 }
 
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
                                               uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
-    using G = PairCfg<BN2, ST>;
+    using G = PairCfg<BN2, ST, SUB>;
     const int eg = warp & 3;
     const uint32_t lane = lane_id();
     uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
@@ -889,9 +902,9 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
     __syncwarp();
 }
 
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __grid_constant__ KParams p) {
-    using G = PairCfg<BN2, ST>;
+    using G = PairCfg<BN2, ST, SUB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -935,12 +948,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     if (warp == 0) {
-        if (lane == 0) pair_loader<BN2, ST>(p, smem, full, empty, crank, dl);
+        if (lane == 0) pair_loader<BN2, ST, SUB>(p, smem, full, empty, crank, dl);
     } else if (warp == 1) {
-        if (lane == 0 && crank == 0) pair_mma<BN2, ST>(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        if (lane == 0 && crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
-        pair_epilogue<BN2, ST>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+        pair_epilogue<BN2, ST, SUB>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
     } else if (p.world > 1) {
         role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
@@ -1015,21 +1028,24 @@ int env_int(const char* name, int dflt) {
 
 namespace {
 
-// The CTA-pair kernel instantiations: tile width x pipeline depth.  The deeper
-// variant of each width trades the epilogue's smem staging for one more stage.
+// The CTA-pair kernel instantiations: tile width x pipeline depth x k sub-blocks
+// per stage.  SUB = 2 (8 MMAs per stage) is the default; SUB = 1 with twice the
+// stages is kept for comparison.
 struct PairKernel {
     const void* fn;
     int smem;
     int bn;
     int stages;
+    int sub;
     bool staged_epilogue;
     int clusters;  // resident CTA pairs on this device
 };
 
-template <int BN2, int ST>
+template <int BN2, int ST, int SUB>
 PairKernel pair_kernel_entry() {
-    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<BN2, ST>), PairCfg<BN2, ST>::SMEM, BN2, ST,
-                      PairCfg<BN2, ST>::STAGED_EPI, 0};
+    using G = PairCfg<BN2, ST, SUB>;
+    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<BN2, ST, SUB>), G::SMEM, BN2, ST, SUB,
+                      G::STAGED_EPI, 0};
 }
 
 constexpr int kNumPairKernels = 4;
@@ -1068,10 +1084,10 @@ int device_info(int dev, const DevInfo** out) {
     if (dev < 0 || dev >= 64) return fail(AGG_EINVAL, "device ordinal %d out of range", dev);
     std::call_once(g_dev_once[dev], [dev] {
         DevInfo& d = g_dev[dev];
-        d.pair[0] = pair_kernel_entry<256, 6>();
-        d.pair[1] = pair_kernel_entry<256, 7>();
-        d.pair[2] = pair_kernel_entry<128, 8>();
-        d.pair[3] = pair_kernel_entry<128, 9>();
+        d.pair[0] = pair_kernel_entry<256, 3, 2>();
+        d.pair[1] = pair_kernel_entry<256, 6, 1>();
+        d.pair[2] = pair_kernel_entry<128, 4, 2>();
+        d.pair[3] = pair_kernel_entry<128, 8, 1>();
         auto setup = [&]() -> int {
             AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
             AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
@@ -1139,10 +1155,10 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
         const long tiles256 = static_cast<long>((a->M + 255) / 256) * ((a->N + 255) / 256);
         int bn = 256;
         if (bn_env == 128 || (bn_env == 0 && (a->N <= 128 || tiles256 < 2L * di->pair[0].clusters))) bn = 128;
-        const int st_env = env_int("AGG_STAGES", 0);
+        const int sub_env = env_int("AGG_SUB", 2);
         for (const PairKernel& k : di->pair)
-            if (k.bn == bn && (st_env ? k.stages == st_env : k.staged_epilogue)) pk = &k;
-        if (!pk) return fail(AGG_EINVAL, "agg_launch: no pair kernel with BN=%d and %d stages", bn, st_env);
+            if (k.bn == bn && k.sub == sub_env) pk = &k;
+        if (!pk) return fail(AGG_EINVAL, "agg_launch: no pair kernel with BN=%d and %d k sub-blocks", bn, sub_env);
         if (pk->clusters < 1) pk = nullptr;
     }
     const int tile_m = pk ? 256 : BM;
@@ -1181,7 +1197,8 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.num_m_tiles = (a->M + tile_m - 1) / tile_m;
     p.num_n_tiles = (a->N + tile_n - 1) / tile_n;
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
-    p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + BK_BYTES - 1) / BK_BYTES);
+    const size_t kblock_bytes = static_cast<size_t>(BK_BYTES) * (pk ? pk->sub : 1);
+    p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + kblock_bytes - 1) / kblock_bytes);
     p.group_m = std::max(1, env_int("AGG_GROUP_M", pk ? 8 : 16));
     p.dtype = a->dtype;
     p.scale_a = a->scale_a;
