@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 MAX_REL_F8 = 3e-2
 
 
-@pytest.fixture(params=["1sm", "pair256", "pair128", "pair256k1"])
+@pytest.fixture(params=["1sm", "pair256", "pair128", "pair256k1", "wide"])
 def f8_variant(request, monkeypatch):
     for k in ENV_KNOBS:
         monkeypatch.delenv(k, raising=False)

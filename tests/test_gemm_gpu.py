@@ -20,7 +20,8 @@ VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
             "pair256": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "2"},
             "pair256k1": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "1"},
             "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "2"},
-            "pair128k1": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "1"}}
+            "pair128k1": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "1"},
+            "wide": {"AGG_KERNEL": "wide"}}
 ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB")
 
 

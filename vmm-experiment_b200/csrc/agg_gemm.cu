@@ -985,6 +985,342 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     }
 }
 
+// ================================================================ wide CTA-pair kernel
+//
+// The pair computes a 256 x 512 tile as two N=256 halves that share every A
+// k-block: per k-step the even CTA issues two tcgen05.mma.cta_group::2, one per
+// half.  Per SM that is 25% fewer operand bytes from L2 per FLOP than the
+// 256 x 256 tile.  The accumulator (128 x 512 fp32 per CTA) fills TMEM, so
+// there is one accumulator; the epilogue releases each half (tempty[0], [1])
+// as soon as it has read it, and the next tile's first MMAs into a half wait
+// only for that half.
+struct WideCfg {
+    static constexpr int TILE_M = 256;
+    static constexpr int TILE_N = 512;
+    static constexpr int A_BYTES = 128 * BK_BYTES;     // 16 KiB
+    static constexpr int B_HALF = 128 * BK_BYTES;      // this CTA's 128 rows of one N half
+    static constexpr int STAGE = A_BYTES + 2 * B_HALF;  // 48 KiB
+    static constexpr int STAGES = 4;
+    static constexpr int EPI_OFF = STAGES * STAGE;
+    static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1;
+    static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
+    static constexpr int SMEM = SLOT_OFF + 16 + 1024;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0, "swizzle alignment");
+};
+
+__device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                            uint32_t crank, const Deadline& dl) {
+    using G = WideCfg;
+    tma_prefetch_desc(&p.tm_a_src);
+    tma_prefetch_desc(&p.tm_b);
+    if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
+    const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used = 0, last_par = 0;
+    bool ok = true;
+    FlagWaitLog log;
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        ++log.tiles;
+        const int row = mt * G::TILE_M + static_cast<int>(crank) * 128;
+        const CUtensorMap* tma = &p.tm_a_src;
+        int a_row = row;
+        if (p.world > 1) {
+            const int src = row / p.m_local;
+            if (src == p.rank) {
+                a_row = row - src * p.m_local;
+            } else {
+                const uint32_t* f = p.flags_uc + src * AGG_MAX_CHUNKS + (row - src * p.m_local) / BM;
+                if (!log.wait(p, f, dl)) {
+                    record_failure(p.status, AGG_ROLE_FLAG, static_cast<uint32_t>(row / BM));
+                    ok = false;
+                    break;
+                }
+                fence_proxy_alias();
+                fence_proxy_async_global();
+                tma = &p.tm_a_gath;
+            }
+        }
+        const int b_row0 = nt * G::TILE_N + static_cast<int>(crank) * 128;  // half 0; half 1 is +256
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait_timed(&empty[stage], phase ^ 1u, dl, p.trace != nullptr, log.stage_wait, log.stage_waits)) {
+                record_failure(p.status, AGG_ROLE_TMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            uint8_t* sa = smem + stage * G::STAGE;
+            uint8_t* sb = sa + G::A_BYTES;
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE);
+            const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+            const int kx = kb * kb_elems;
+            tma_load_2d_pair(tma, sa, bar, kx, a_row);
+            tma_load_2d_pair(&p.tm_b, sb, bar, kx, b_row0);
+            tma_load_2d_pair(&p.tm_b, sb + G::B_HALF, bar, kx, b_row0 + 256);
+            used |= 1u << stage;
+            last_par = (last_par & ~(1u << stage)) | (phase << stage);
+            if (++stage == G::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+    log.flush(p);
+    if (crank == 0)
+        for (int s = 0; s < G::STAGES; ++s)
+            if (used & (1u << s))
+                if (!mbar_wait_for(&full[s], (last_par >> s) & 1u, 200000000ull))
+                    record_failure(p.status, AGG_ROLE_DRAIN, 1u);
+}
+
+__device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                         const Deadline& dl) {
+    using G = WideCfg;
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, 256) : make_idesc(1, 1, G::TILE_M, 256);
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
+                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+                ok = false;
+                break;
+            }
+            const uint32_t sa = smem_u32(smem + stage * G::STAGE);
+            const uint64_t adesc = sw128_kmajor_desc(sa);
+            const uint64_t bdesc0 = sw128_kmajor_desc(sa + G::A_BYTES);
+            const uint64_t bdesc1 = sw128_kmajor_desc(sa + G::A_BYTES + G::B_HALF);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t off = static_cast<uint64_t>(k * 2);
+                const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (kb == 0 && k == 0) {
+                        // the epilogue must have read this half of the previous tile
+                        if (!mbar_wait_timed(&tempty[h], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
+                            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(h * 256);
+                    const uint64_t bd = (h ? bdesc1 : bdesc0) + off;
+                    if (f8)
+                        umma_f8_pair(d, adesc + off, bd, idesc, accumulate);
+                    else
+                        umma_f16_pair(d, adesc + off, bd, idesc, accumulate);
+                }
+                if (!ok) break;
+            }
+            if (!ok) break;
+            umma_commit_pair_mc(&empty[stage], 0x3);
+            if (++stage == G::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(tfull, 0x3);
+        acc_phase ^= 1u;
+    }
+    umma_commit_pair_mc(drain, 0x1);
+    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+    if (p.trace) {
+        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+        trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
+        trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
+        trace_set(p, AGG_TR_MMA_STALLS, full_waits);
+    }
+}
+
+__device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
+                                              uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
+    using G = WideCfg;
+    const int eg = warp & 3;
+    const uint32_t lane = lane_id();
+    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
+    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
+    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    uint32_t acc_phase = 0;
+    int buf = 0;
+    for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        int got = 1;
+        if (lane == 0) got = mbar_wait_sleepy(tfull, acc_phase, dl) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, static_cast<uint32_t>(t));
+            break;
+        }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
+        const int row0 = mt * G::TILE_M + static_cast<int>(crank) * 128 + eg * 32;
+        const float row_scale = f8 ? epilogue_row_scale(p, row0, lane, dl) : 1.0f;
+#pragma unroll 1
+        for (int j = 0; j < G::TILE_N / EPI_COLS; ++j) {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS), r0);
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS + 32), r1);
+            tmem_wait_ld();
+            if ((j & 3) == 3) {
+                // this N half is read: the next tile may accumulate into it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[j >> 2]), 0));
+            }
+            const int col0 = nt * G::TILE_N + j * EPI_COLS;
+            uint32_t packed[32];
+            if (f8) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]) * row_scale * s0,
+                                            __uint_as_float(r0[2 * i + 1]) * row_scale * s1);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c = col0 + 32 + 2 * i;
+                    const float s0 = c < p.N ? __ldg(p.scale_b + c) : 0.0f;
+                    const float s1 = c + 1 < p.N ? __ldg(p.scale_b + c + 1) : 0.0f;
+                    packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]) * row_scale * s0,
+                                                 __uint_as_float(r1[2 * i + 1]) * row_scale * s1);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+            }
+            if (col0 < p.N) {
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                uint8_t* b = stg + buf * EPI_BUF_BYTES;
+                const uint32_t row_base = smem_u32(b) + lane * 128u;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t addr = row_base + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * c]),
+                                 "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
+                                 : "memory");
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&p.tm_c, b, col0, row0);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            }
+        }
+        acc_phase ^= 1u;
+    }
+    if (lane == 0) {
+        bulk_wait_group<0>();
+        if (p.trace) trace_max(p, AGG_TR_EPI_DONE, globaltimer_ns());
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __grid_constant__ KParams p) {
+    using G = WideCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::BAR_OFF);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + G::STAGES;
+    uint64_t* tfull = bars + 2 * G::STAGES;
+    uint64_t* tempty = tfull + 1;  // [2]: one per N half
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::SLOT_OFF);
+
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const uint32_t lane = lane_id();
+    const uint32_t crank = cluster_ctarank();
+    Deadline dl;
+    dl.end_ns = globaltimer_ns() + (p.timeout_ns ? p.timeout_ns : 10000000000ull);
+    dl.status = p.status;
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_START, globaltimer_ns());
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        mbar_init(&tempty[0], 2 * EPI_WARPS);
+        mbar_init(&tempty[1], 2 * EPI_WARPS);
+        mbar_init(drain, 1);
+        fence_mbarrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, G::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+    if (warp == 0) {
+        if (lane == 0) wide_loader(p, smem, full, empty, crank, dl);
+    } else if (warp == 1) {
+        if (lane == 0 && crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        __syncwarp();
+    } else if (warp < 2 + EPI_WARPS) {
+        wide_epilogue(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+    } else if (p.world > 1) {
+        role_producer(p, warp - 2 - EPI_WARPS, dl);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (failed(p.status)) {
+        const uint64_t until = globaltimer_ns() + 2000000ull;
+        while (globaltimer_ns() < until) {
+        }
+    }
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, G::TMEM_COLS);
+    }
+    if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_END, globaltimer_ns());
+    if (p.world > 1 && threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t prev = atomicAdd(p.cta_counter, 1u);
+        if (prev == gridDim.x - 1u) {
+            atomicExch(p.cta_counter, 0u);
+            atomicExch(p.ticket, 0ull);
+            fence_acq_rel_sys();
+            mm_red_add_release_u32(p.done_mc, 1u);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- host side
 namespace {
 
@@ -1034,21 +1370,28 @@ namespace {
 struct PairKernel {
     const void* fn;
     int smem;
-    int bn;
+    int bn;      // output columns per pair tile
+    int b_box;   // B rows one CTA loads per TMA box
     int stages;
-    int sub;
-    bool staged_epilogue;
+    int sub;     // 128-byte k sub-blocks per stage
+    bool wide;   // 256 x 512 tile with one accumulator
+    float cost;  // relative time per output element (measured on the 70B MLP shape)
     int clusters;  // resident CTA pairs on this device
 };
 
 template <int BN2, int ST, int SUB>
-PairKernel pair_kernel_entry() {
+PairKernel pair_kernel_entry(float cost) {
     using G = PairCfg<BN2, ST, SUB>;
-    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<BN2, ST, SUB>), G::SMEM, BN2, ST, SUB,
-                      G::STAGED_EPI, 0};
+    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<BN2, ST, SUB>), G::SMEM, BN2, BN2 / 2, ST, SUB,
+                      false, cost, 0};
 }
 
-constexpr int kNumPairKernels = 4;
+PairKernel wide_kernel_entry(float cost) {
+    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_wide_kernel), WideCfg::SMEM, WideCfg::TILE_N, 128,
+                      WideCfg::STAGES, 1, true, cost, 0};
+}
+
+constexpr int kNumPairKernels = 5;
 
 // Per-device launch facts, filled once: SM count and how many CTA pairs of each
 // pair kernel can be resident at once (clusters must fit inside a GPC).
@@ -1084,10 +1427,15 @@ int device_info(int dev, const DevInfo** out) {
     if (dev < 0 || dev >= 64) return fail(AGG_EINVAL, "device ordinal %d out of range", dev);
     std::call_once(g_dev_once[dev], [dev] {
         DevInfo& d = g_dev[dev];
-        d.pair[0] = pair_kernel_entry<256, 3, 2>();
-        d.pair[1] = pair_kernel_entry<256, 6, 1>();
-        d.pair[2] = pair_kernel_entry<128, 4, 2>();
-        d.pair[3] = pair_kernel_entry<128, 8, 1>();
+        // relative cost per output element, from sustained runs of each variant
+        d.pair[0] = pair_kernel_entry<256, 3, 2>(1.00f);
+        d.pair[1] = pair_kernel_entry<256, 6, 1>(1.08f);
+        d.pair[2] = pair_kernel_entry<128, 4, 2>(1.35f);
+        d.pair[3] = pair_kernel_entry<128, 8, 1>(1.45f);
+        // The wide tile reads 21% fewer L2 sectors but exposes its epilogue (one
+        // accumulator): measured slower on the 70B shapes, so it is chosen only
+        // when asked for (AGG_KERNEL=wide).
+        d.pair[4] = wide_kernel_entry(1.40f);
         auto setup = [&]() -> int {
             AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
             AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
@@ -1144,26 +1492,38 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     int rc = device_info(dev, &di);
     if (rc) return rc;
 
-    // ---- kernel choice: the CTA-pair kernel unless the shard height forbids it.
-    // Tile width 256 unless that leaves fewer than two waves of tiles; the
-    // deeper pipeline variant (AGG_STAGES) for A/B measurement.
+    // ---- kernel choice.  A CTA-pair kernel unless the shard height forbids it
+    // (a 256-row tile must not straddle two shards); among them the one with the
+    // smallest estimated time = waves of tiles x tile area x relative cost, so
+    // that wave quantisation of small problems is weighed against efficiency.
+    // AGG_KERNEL=1sm|pair|wide, AGG_BN=128|256 and AGG_SUB=1|2 override it.
     const PairKernel* pk = nullptr;
     const char* kenv = getenv("AGG_KERNEL");
     const bool force_1sm = kenv && std::strcmp(kenv, "1sm") == 0;
-    if (!force_1sm && !(world > 1 && m_local % 256) && di->pair[0].clusters >= 1) {
+    const bool force_wide = kenv && std::strcmp(kenv, "wide") == 0;
+    const bool force_pair = kenv && std::strcmp(kenv, "pair") == 0;
+    if (!force_1sm && !(world > 1 && m_local % 256)) {
         const int bn_env = env_int("AGG_BN", 0);
-        const long tiles256 = static_cast<long>((a->M + 255) / 256) * ((a->N + 255) / 256);
-        int bn = 256;
-        if (bn_env == 128 || (bn_env == 0 && (a->N <= 128 || tiles256 < 2L * di->pair[0].clusters))) bn = 128;
         const int sub_env = env_int("AGG_SUB", 2);
-        for (const PairKernel& k : di->pair)
-            if (k.bn == bn && k.sub == sub_env) pk = &k;
-        if (!pk) return fail(AGG_EINVAL, "agg_launch: no pair kernel with BN=%d and %d k sub-blocks", bn, sub_env);
-        if (pk->clusters < 1) pk = nullptr;
+        double best = 0.0;
+        for (const PairKernel& k : di->pair) {
+            if (k.clusters < 1) continue;
+            if (force_wide && !k.wide) continue;
+            if (force_pair && k.wide) continue;
+            if (!k.wide && (k.sub != sub_env || (bn_env && k.bn != bn_env))) continue;
+            if (k.wide && (bn_env || sub_env != 2)) continue;
+            const long tiles = static_cast<long>((a->M + 255) / 256) * ((a->N + k.bn - 1) / k.bn);
+            const long waves = (tiles + k.clusters - 1) / k.clusters;
+            const double est = static_cast<double>(waves) * 256.0 * k.bn * k.cost;
+            if (!pk || est < best) {
+                pk = &k;
+                best = est;
+            }
+        }
     }
     const int tile_m = pk ? 256 : BM;
     const int tile_n = pk ? pk->bn : BN;
-    const int b_box = pk ? tile_n / 2 : BN;
+    const int b_box = pk ? pk->b_box : BN;
 
     KParams p;
     std::memset(&p, 0, sizeof(p));
