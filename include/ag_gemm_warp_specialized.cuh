@@ -75,7 +75,7 @@ DT distributed_tensor_from_data_ptr(uint64_t mc, uint64_t* peers, int b, int d, 
 
 namespace ag_gemm_warp_specialized {
 
-template <int BM, int BN, int C>
+template <int BM, int BN, int NC>
 struct fused_globals {
     using A_distributed_tensor = dist::distributed_tensor<comm::bf16>;
     using A_local_tensor = dist::local_tensor<comm::bf16>;
@@ -98,8 +98,8 @@ inline size_t gather_offset(size_t shard_bytes) { return (shard_bytes + (2u << 2
 
 }  // namespace ag_gemm_warp_specialized
 
-template <int BM, int BN, int C, int S>
-int launch_ag_gemm_warp_specialized(const ag_gemm_warp_specialized::fused_globals<BM, BN, C>& g,
+template <int BM, int BN, int NC, int S>
+int launch_ag_gemm_warp_specialized(const ag_gemm_warp_specialized::fused_globals<BM, BN, NC>& g,
                                     cudaStream_t stream = nullptr) {
     const int rank = g.dev_idx;
     const RankState& rs = g_rs[rank];
