@@ -15,14 +15,16 @@ pytestmark = pytest.mark.gpu
 MAX_REL = 1e-2
 
 # Kernel variants selectable at launch time: the one-CTA kernel (128 x 256 tiles)
-# and the CTA-pair kernel (256 x 256 or 256 x 128 tiles).
+# and the CTA-pair kernel (256 x 256 or 256 x 128 tiles), in m-major and
+# n-major tile order.
 VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
             "pair256": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "2"},
             "pair256k1": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "1"},
             "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "2"},
             "pair128k1": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "1"},
-            "wide": {"AGG_KERNEL": "wide"}}
-ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB")
+            "wide": {"AGG_KERNEL": "wide"},
+            "pair256n": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_RASTER_N": "1", "AGG_GROUP_M": "3"}}
+ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB", "AGG_RASTER_N", "AGG_GROUP_M")
 
 
 @pytest.fixture(params=sorted(VARIANTS))
