@@ -209,6 +209,25 @@ int agg_gemm_e4m3(const void* A, const void* B, void* C, const float* scale_a,
 /* Number of SMs the persistent grid uses on the current device (0 on failure). */
 int agg_num_sms(void);
 
+/* Single-GPU bf16 GEMM, C[M,N] = A[M,K] . B[N,K]^T, that allocates nothing: for
+   callers that may not call cudaMalloc (a plugin inside a program whose caching
+   allocator owns all device memory, a loop that must not take the allocator's
+   device-wide synchronisation).  No counterpart in the reference.
+   K is split into `splits` ranges (0 = chosen from the SM count); the fp32
+   partial tiles and their arrival counters live in one static device array of
+   AGG_NOALLOC_SCRATCH_BYTES that every GPU whose context loads this library's
+   kernels holds until exit.  Limit: (ceil(M/128) * ceil(N/256)) * splits <= 255
+   and splits <= ceil(K/64); larger requests return AGG_EINVAL with the bytes
+   they would need.  Same shape rules as agg_gemm_bf16, and A, B, C 16-byte aligned.
+   The first call on a device looks up the array's device address (with that
+   device current); make that first call before any stream capture.  All calls
+   on a device share the array and it keeps the last call's contents: each call
+   first clears the counters it uses, so calls whose executions overlap on the
+   GPU (concurrent streams) race and must be serialised by the caller. */
+#define AGG_NOALLOC_SCRATCH_BYTES (32u << 20)
+int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int splits,
+                          uint32_t* status, void* stream);
+
 /* ---- multicast primitives ---------------------------------------------------------- */
 /* Broadcast `bytes` (multiple of 16) from local `src` to `mc_dst` with 16-byte
    multimem.st, then raise the u32 at `flag_mc` by one (release, system scope)

@@ -72,7 +72,7 @@ EXPORTS = [
     "agg_launch", "agg_gemm_bf16", "agg_gemm_e4m3", "agg_num_sms",
     "agg_mc_broadcast", "agg_verify_bytes", "agg_verify_pattern_gather", "agg_alias_fence",
     "agg_multimem_ops_test", "agg_multimem_ld_reduce_v4", "agg_multimem_red_add_v4",
-    "agg_mm_barrier", "agg_wait_flag",
+    "agg_mm_barrier", "agg_wait_flag", "agg_gemm_bf16_noalloc",
 ]
 
 
@@ -164,6 +164,7 @@ def lib() -> ctypes.CDLL:
         "agg_multimem_red_add_v4": ([u64, ctypes.c_float, sz, vp], i32),
         "agg_mm_barrier": ([vp, vp, i32, u32, i32, vp, u64, vp], i32),
         "agg_wait_flag": ([vp, u32, vp, u64, vp], i32),
+        "agg_gemm_bf16_noalloc": ([vp, vp, vp, i32, i32, i32, i32, vp, vp], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
