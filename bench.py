@@ -12,6 +12,10 @@ of C_r = AllGather(A_r) . B_r^T over the workload's shapes on every rank:
   qkv8b             Llama-3-8B QKV projection: M = 8192, K = 4096, N = 6144;
   smoke             M = 1024, K = 1024, N = 1024.
 
+--op rs times the row-parallel twin instead (GEMM + reduce-scatter):
+  mlp70b_down       Llama-3-70B MLP down projection: M = 16384, K = 28672
+                    (28672/N per rank), N = 8192; rank r keeps rows r of the sum.
+
 Inputs are synthetic, seeded per rank on the device: activations ~ N(0, 1),
 weights ~ N(0, 0.02).  They are larger than L2 at mlp70b/qkv8b, so no flush
 is inserted between timed steps (smoke flushes L2 with a 256 MiB write).
@@ -49,6 +53,8 @@ WORKLOADS = {
     # a 4096-row x 8192-column slice of mlp70b (256 MB of operands): the case
     # the ncu captures run on
     "mlp70b_slice": dict(name="llama3-70b-mlp-slice", M=4096, K=8192, N=8192),
+    # the row-parallel twin (--op rs): Llama-3-70B MLP down projection, K split over ranks
+    "mlp70b_down": dict(name="llama3-70b-mlp-down", M=16384, K=28672, N=8192),
 }
 NVLINK_GBS = 770.0        # measured peer copy per direction on this pool
 FALLBACK_HBM_GBS = 6650.0
@@ -159,7 +165,8 @@ def run_reference(args, rank, emit):
     tflops = 2.0 * rows * cols * K / dt / 1e12
     sample = f"{rows} rows x {cols} cols x K={K} of the {w['name']} GEMM per step (fp32, {threads} threads)"
     line = {
-        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
+        "impl": "reference", "metric": RS_METRIC if args.op == "rs" else METRIC, "value": tflops,
+        "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_of(args.workload, world),
@@ -208,6 +215,139 @@ def cpu_baseline(workload):
             "sample": f"{reps} x ({rows} x {cols} x K={K}) slices of the {w['name']} GEMM, fp32, {el:.1f} s"}
 
 
+RS_METRIC = "GEMM + reduce-scatter TFLOP/s per GPU at 1/2/4/8 B200; % of roofline; vs cuBLAS+NCCL"
+
+
+def run_rs(args, pkg, rank, world, dev, host_group, emit):
+    """The row-parallel twin: Y_r = rows r of sum_s X_s . W_s^T, K split over the
+    ranks.  A step is one launch on every rank; the unfused baseline is a cuBLAS
+    GEMM to a full [M, N] bf16 partial followed by an NCCL reduce-scatter."""
+    import torch
+    import torch.distributed as dist
+
+    w = WORKLOADS[args.workload]
+    M, Ktot, N = w["M"], w["K"], w["N"]
+    k_r, m_local = Ktot // world, M // world
+    g = torch.Generator(device=dev).manual_seed(1000 * rank + 9)
+    X_r = torch.randn(M, k_r, device=dev, generator=g).bfloat16()
+    W_r = (torch.randn(N, k_r, device=dev, generator=g) * 0.02).bfloat16()
+    Y_r = torch.empty(m_local, N, device=dev, dtype=torch.bfloat16)
+    op = pkg.GemmReduceScatter(M, N, k_r, host_group=host_group)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=host_group)
+
+    def timed(step_fn, steps):
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step_fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=host_group)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        op(X_r, W_r, out=Y_r)
+    torch.cuda.synchronize()
+    op.check_status()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    ms = timed(lambda: op(X_r, W_r, out=Y_r), args.steps)
+    clk = clocks.stop()
+    op.check_status()
+
+    flops_rank = 2.0 * M * N * k_r
+    value = flops_rank * world / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    t_tc = flops_rank / (peaks["bf16"] * 1e12)
+    nvl_bytes = (world - 1) / world * M * N * 2 if world > 1 else 0.0   # partials leaving each GPU
+    t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
+    t_roof = max(t_tc, t_nvl)
+    roofline = {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "achieved": flops_rank / (ms * 1e-3) / 1e12,
+                "peak": peaks["bf16"], "unit": "TFLOP/s", "frac": t_roof / (ms * 1e-3),
+                "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)", "traffic": None,
+                "t_roof_ms": t_roof * 1e3, "t_tensor_ms": t_tc * 1e3, "t_nvlink_ms": t_nvl * 1e3,
+                "nvlink_bytes_per_rank": nvl_bytes, "nvlink_gbs": NVLINK_GBS}
+    out = {"metric": RS_METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (X~N(0,1), W~N(0,0.02), seeded per rank)",
+           "config": {"workload": w["name"], "M": M, "K_total": Ktot, "K_per_rank": k_r, "N": N,
+                      "M_out_per_rank": m_local, "P": world, "l2": "inputs larger than L2, no flush",
+                      "parallelism": f"rs-tp{world}"},
+           "tflops_per_gpu": value / world, "gpu_launches": args.steps, "roofline": roofline, "clocks": clk}
+
+    if not args.no_unfused:
+        P_full = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        Y_u = torch.empty(m_local, N, device=dev, dtype=torch.bfloat16)
+
+        def step_unfused():
+            torch.matmul(X_r, W_r.t(), out=P_full)
+            if world > 1:
+                dist.reduce_scatter_tensor(Y_u, P_full)
+            else:
+                Y_u.copy_(P_full)
+
+        for _ in range(args.warmup):
+            step_unfused()
+        ums = timed(step_unfused, args.steps)
+        out["unfused_nccl_cublas"] = {"value": flops_rank * world / (ums * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                      "ms_per_step": ums, "speedup_fused": ums / ms}
+        if world > 1:
+            # same inputs, same reduction: the fused rows against NCCL's (bf16 partials both ways)
+            ref = Y_u.float()
+            out["unfused_max_rel_diff"] = float(((Y_r.float() - ref).abs().max() / ref.abs().max()).item())
+        del P_full, Y_u
+
+    if not args.no_e2e:
+        X_host = torch.empty(M, k_r, dtype=torch.bfloat16, pin_memory=True)
+        X_host.copy_(X_r)
+        Y_host = torch.empty(m_local, N, dtype=torch.bfloat16, pin_memory=True)
+        X_dev = torch.empty_like(X_r)
+
+        def step_e2e():
+            X_dev.copy_(X_host, non_blocking=True)
+            op(X_dev, W_r, out=Y_r)
+            Y_host.copy_(Y_r, non_blocking=True)
+
+        step_e2e()
+        e2e_steps = max(2, min(args.steps, 5))
+        ems = timed(step_e2e, e2e_steps)
+        out["e2e"] = {"value": flops_rank * world / (ems * 1e-3) / 1e12, "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": X_host.numel() * 2, "d2h_bytes_per_step": Y_host.numel() * 2,
+                      "ms_per_step": ems, "steps": e2e_steps, "gpu_launches": e2e_steps}
+        op.check_status()
+
+    if args.trace and world > 1:
+        tr = op.new_trace()
+        torch.cuda.synchronize()
+        barrier()
+        op(X_r, W_r, out=Y_r, trace=tr)
+        torch.cuda.synchronize()
+        op.check_status()
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, tr.cpu().numpy(), group=host_group)
+        if rank == 0:
+            with open(args.trace, "w") as f:
+                json.dump({"workload": out["config"], "ranks": [pkg.agg.trace_summary(r) for r in per_rank]}, f,
+                          indent=1)
+
+    op.close()
+    if rank == 0:
+        emit(out)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -224,7 +364,12 @@ def main():
     ap.add_argument("--sweep-max", type=int, default=1 << 30)
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
+    ap.add_argument("--op", default="ag", choices=["ag", "rs"],
+                    help="ag: the all-gather GEMM (default); rs: its GEMM + reduce-scatter twin "
+                         "(default workload mlp70b_down)")
     args = ap.parse_args()
+    if args.op == "rs" and args.workload == "mlp70b":
+        args.workload = "mlp70b_down"
     args.warmup = max(args.warmup, 3)
     # Library banners (NCCL, ...) go to stderr: stdout carries only the result line.
     sys.stdout.flush()
@@ -284,6 +429,10 @@ def main():
             emit({"sweep": "multicast multimem.st write bandwidth", "n_gpus": world, "unit": "GB/s",
                   "rows": rows})
         dist.destroy_process_group()
+        return
+
+    if args.op == "rs":
+        run_rs(args, pkg, rank, world, dev, host_group, emit)
         return
 
     w = WORKLOADS[args.workload]

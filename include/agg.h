@@ -61,6 +61,7 @@ extern "C" {
 #define AGG_ROLE_PROD 5u       /* multicast producer waiting for the previous launch  */
 #define AGG_ROLE_BARRIER 6u    /* mm_barrier gave up                                  */
 #define AGG_ROLE_DRAIN 7u      /* teardown wait for in-flight copies / MMAs          */
+#define AGG_ROLE_REDUCE 8u     /* reduce-scatter: reducer waiting for a tile's partials */
 
 /* ---- dtypes ----------------------------------------------------------------------- */
 #define AGG_DTYPE_BF16 0
@@ -78,12 +79,25 @@ extern "C" {
                                        /* launch); +64 B: this GPU's CTA counter;        */
                                        /* +4 KiB: u32 [AGG_MAX_CHUNKS] producer counters */
 #define AGG_FLAG_USER_OFF (72u << 10)  /* free for mm_barrier rows / tests (56 KiB)      */
+#define AGG_RS_MAX_TILES 8192          /* reduce-scatter: the chunk-counter area holds   */
+                                       /* u32 [2][AGG_RS_MAX_TILES] per-tile counters    */
 
 /* agg_args.flags bits */
 #define AGG_ARGS_DOUBLE_BUFFER 1u      /* gathered A has two [M, K] regions used by     */
                                        /* launch parity (A_local_buf / A_mc point at    */
                                        /* region 0, region 1 follows), so a launch never */
                                        /* waits for the other ranks' previous launch    */
+/* Who moves this rank's shard (default: the kernel's own producer warps, multimem.st).
+   The copy-engine modes (vmm/test_vmm_multicast_speed.cu:172-263) leave the SMs to the
+   GEMM: an internal stream, ordered after the caller's prior work on `stream`, copies
+   the shard in chunk order with cudaMemcpyAsync and raises each chunk's flag on every
+   GPU with cuStreamWriteValue32 through the peers' unicast mappings (A_peer[]); the
+   launch completes on `stream` once the copies have.  They need
+   AGG_ARGS_DOUBLE_BUFFER, bf16, A_peer[s] = every rank's slab base as mapped here
+   (A_peer[rank] = this GPU's, containing A_copy_ready), and consecutive launches on
+   one slab issued on the same stream. */
+#define AGG_ARGS_CE_MC_PUSH 2u         /* one copy per chunk into the multicast VA       */
+#define AGG_ARGS_CE_PEER_PUSH 4u       /* one copy per chunk and peer (order r-1, r-2..) */
 
 /* Per-rank view of the multicast slab (RankState of the reference, C layout). */
 typedef struct agg_rank_info {
@@ -227,6 +241,65 @@ int agg_num_sms(void);
 #define AGG_NOALLOC_SCRATCH_BYTES (32u << 20)
 int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, int K, int splits,
                           uint32_t* status, void* stream);
+
+/* ---- the fused GEMM + reduce-scatter (row-parallel twin) ---------------------------- */
+/*
+ * Y_r[M/P, N] = rows [r*M/P, (r+1)*M/P) of  sum_s X_s[M, K_s] . W_s[N, K_s]^T
+ * (bf16 in, fp32 accumulate, bf16 partials, fp32 sum, bf16 out), in one kernel per
+ * rank: the tensor-core warps compute every [256 x 256] tile of this rank's
+ * partial product into its slab and raise the tile's counter on every GPU
+ * (multimem.red); reducer warps on the owning rank pull the sum of all ranks'
+ * copies of its tiles through NVSwitch (multimem.ld_reduce.add.acc::f32) as the
+ * tiles complete.  The reduce-scatter channels that the reference's RankState
+ * reserves (rs_calls, dmw_cnt[kDmwChannels]; include/multimem.cuh:13-17) have no
+ * kernel in the reference; this is that path.
+ * Shapes: M % P == 0, (M/P) % 256 == 0, N % 8 == 0, K % 8 == 0,
+ * ceil(M/256) * ceil(N/256) <= AGG_RS_MAX_TILES.
+ * Slab data: one [M, N] bf16 partial region (two with AGG_ARGS_DOUBLE_BUFFER,
+ * region 1 right after region 0).  Counters and the done counter live in the
+ * slab's flag area (AGG_FLAG_CHUNK_OFF, AGG_FLAG_DONE_OFF).
+ */
+typedef struct agg_rs_args {
+    const void* X;        /* this rank's activation slice [M, K] bf16, K-major       */
+    const void* W;        /* this rank's weight slice [N, K] bf16, K-major           */
+    void* Y;              /* this rank's rows of the sum [M/world, N] bf16           */
+    uint64_t part_uc;     /* partial region 0, this GPU's unicast VA                  */
+    uint64_t part_mc;     /* partial region 0, multicast VA                           */
+    uint32_t* cnt_uc;     /* per-tile counters (flag area + AGG_FLAG_CHUNK_OFF), UC   */
+    uint32_t* cnt_mc;     /* the same, multicast VA                                   */
+    uint32_t* done_uc;    /* end-of-launch counter (flag area + AGG_FLAG_DONE_OFF), UC */
+    uint32_t* done_mc;    /* the same, multicast VA                                   */
+    uint32_t epoch;       /* launch ordinal on this slab: 1, 2, ... on every rank     */
+    int32_t rank, world;
+    int32_t M, N, K;      /* K: this rank's slice of the contraction                  */
+    uint32_t flags;       /* AGG_ARGS_DOUBLE_BUFFER                                   */
+    uint32_t* status;     /* device status word, may be NULL                          */
+    uint64_t timeout_ns;  /* bound on every device-side wait; 0 = 10 s                */
+    uint64_t* trace;      /* optional: u64 [grid][AGG_TRACE_SLOTS] event times (ns)   */
+} agg_rs_args;
+
+/* Enqueue one launch on `stream`; AGG_EINVAL without launching on bad arguments. */
+int agg_launch_rs(const agg_rs_args* args, void* stream);
+/* sizeof(agg_rs_args), for bindings to check their layout. */
+size_t agg_rs_args_size(void);
+
+/* ---- copy-engine all-gather (vmm/test_vmm_multicast_speed.cu:172-263) ---------------- */
+#define AGG_CE_MC_PUSH 0     /* one cudaMemcpyAsync of the shard into the multicast VA
+                                (enqueue_multicast_push, :183-194)                       */
+#define AGG_CE_PEER_PUSH 1   /* one copy into every peer's slot, destinations r-1, r-2, ...
+                                (enqueue_quack_ag_push, :207-231)                          */
+#define AGG_CE_PEER_PULL 2   /* one copy from every peer's slot into this GPU's, sources
+                                r+1, r+2, ... (enqueue_mkernel_ag_pull, :233-254); the
+                                peers' shards must already be in their own slots           */
+/* Copy-engine all-gather of `shard_bytes` per rank into slot `rank` (offset
+   region_off + rank * shard_bytes) of every rank's slab, on `stream`.  `src` is
+   this rank's shard (PUSH modes; the local slot is filled too).  Uses the slab
+   addresses of `info` (agg_spmm_init / agg_mp_bind). */
+int agg_ce_allgather(const agg_rank_info* info, uint64_t region_off, const void* src, size_t shard_bytes,
+                     int mode, void* stream);
+/* cuStreamWriteValue32 of `value` to a local or peer (unicast) address on `stream`
+   (enqueue_stream_write_value, :256-263): the copy-engine path's flag write. */
+int agg_stream_write_u32(uint64_t addr, uint32_t value, void* stream);
 
 /* ---- multicast primitives ---------------------------------------------------------- */
 /* Broadcast `bytes` (multiple of 16) from local `src` to `mc_dst` with 16-byte

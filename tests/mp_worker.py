@@ -58,8 +58,9 @@ def _bits_to_dev(bits, shape):
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16).reshape(shape)).view(torch.bfloat16).cuda()
 
 
-def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme, double_buffer=True):
-    """Fused all-gather GEMM vs the oracle on the reference harness's inputs."""
+def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme, double_buffer=True, producer="sm"):
+    """Fused all-gather GEMM vs the oracle on the reference harness's inputs
+    (`producer`: who moves the shards, the kernel's warps or the copy engines)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -72,7 +73,8 @@ def ag_gemm_parity(rank, world, port, m_local, k, n_r, launches, scheme, double_
         A_bits, A_ref, B_bits, B_ref = oracle.harness_inputs(world, m_local, k, n_r, scheme)
         A_r = _bits_to_dev(A_bits[rank], (m_local, k))
         B_r = _bits_to_dev(B_bits[rank], (n_r, k))
-        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD, double_buffer=double_buffer)
+        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD, double_buffer=double_buffer,
+                               producer=producer)
         outs = []
         for _ in range(launches):
             C = op(A_r, B_r)
@@ -135,17 +137,18 @@ def ag_gemm_e4m3_parity(rank, world, port, m_local, k, n_r, launches):
         _teardown(op)
 
 
-def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches):
+def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches, producer="sm"):
     """Back-to-back launches with different activations: each output must match
     its own inputs (checks the end-of-launch barrier that guards the gathered
-    buffer against being overwritten while a slower rank still reads it)."""
+    buffer against being overwritten while a slower rank still reads it, or,
+    with copy-engine producers, the stream ordering that stands in for it)."""
     import torch
     import torch.distributed as dist
 
     pkg = _init(rank, world, port)
     op = None
     try:
-        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
+        op = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD, producer=producer)
         g = torch.Generator(device="cuda").manual_seed(rank)
         B_r = (torch.randn(n_r, k, device="cuda", generator=g) * 0.05).bfloat16()
         outs = []
@@ -171,9 +174,60 @@ def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches):
         _teardown(op)
 
 
-def multicast_sweep(rank, world, port, sizes, reps=1):
-    """Each rank pushes `size` bytes into its slot via multimem.st; every rank's
-    copy of every slot must be byte-identical to the sender's source."""
+def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=True):
+    """Fused GEMM + reduce-scatter vs the oracle: launch e uses X_s, W_s drawn by
+    fill_random from seeds 5000 + 100e + s and 6000 + s (U[-1, 1], bf16); rank r's
+    output must be rows [r*M/P, (r+1)*M/P) of sum_s X_s . W_s^T."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+
+    pkg = _init(rank, world, port)
+    op = None
+    try:
+        M = world * m_per_rank
+        Ws = [oracle.fill_random_bf16(6000 + s, n * k) for s in range(world)]
+        op = pkg.GemmReduceScatter(M, n, k, host_group=dist.group.WORLD, double_buffer=double_buffer)
+        W_r = _bits_to_dev(Ws[rank][0], (n, k))
+        outs, inputs = [], []
+        for e in range(launches):
+            Xs = [oracle.fill_random_bf16(5000 + 100 * e + s, M * k) for s in range(world)]
+            inputs.append(Xs)
+            X_r = _bits_to_dev(Xs[rank][0], (M, k))
+            outs.append(op(X_r, W_r))
+        torch.cuda.synchronize()
+        op.check_status()
+        worst, bad_total, bound_total, nan_total = 0.0, 0, 0, 0
+        rows = slice(rank * m_per_rank, (rank + 1) * m_per_rank)
+        for e in range(launches):
+            parts = [oracle.gemm_f64(inputs[e][s][1].reshape(M, k)[rows], Ws[s][1].reshape(n, k))
+                     for s in range(world)]
+            want64 = sum(parts)
+            want = want64.astype(np.float32)
+            got = outs[e].float().cpu().numpy()
+            stats = oracle.error_stats(got, want)
+            bad, _ = oracle.check_close(got, want)
+            # Each rank's partial is rounded to bf16 before the sum (as in a bf16
+            # reduce-scatter): up to 2^-9 of every |partial| on top of the
+            # reference's element check (atol 0.1, rtol 0.02).
+            tol = 0.1 + 0.02 * np.abs(want64) + 2.0 ** -8 * sum(np.abs(p) for p in parts)
+            bound_total += int(np.count_nonzero(~(np.abs(got - want64) <= tol)))
+            worst = max(worst, stats["max_rel_err"])
+            bad_total += bad
+            nan_total += stats["nan"]
+        return {"rank": rank, "worst_rel_err": worst, "bad_check_close": bad_total, "bad": bound_total,
+                "nan": nan_total, "epoch": op.epoch}
+    finally:
+        _teardown(op)
+
+
+def multicast_sweep(rank, world, port, sizes, reps=1, mode="sm"):
+    """Each rank moves `size` bytes into its slot on every GPU -- mode "sm":
+    multimem.st (agg_mc_broadcast); "ce_mc" / "ce_push" / "ce_pull": the copy
+    engines (agg_ce_allgather) -- and every rank's copy of every slot must be
+    byte-identical to the sender's source."""
     import ctypes
 
     import torch
@@ -195,16 +249,28 @@ def multicast_sweep(rank, world, port, sizes, reps=1):
                 return (torch.rand(size // 2, device="cuda", generator=g) * 2 - 1).bfloat16()
 
             src = src_of(rank)
+            ce = {"ce_mc": agg.AGG_CE_MC_PUSH, "ce_push": agg.AGG_CE_PEER_PUSH, "ce_pull": agg.AGG_CE_PEER_PULL}
+
+            def move():
+                if mode == "sm":
+                    agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None,
+                                                 0, stream))
+                else:
+                    agg.check(L.agg_ce_allgather(ctypes.byref(slab.info), 0, ctypes.c_void_p(src.data_ptr()), size,
+                                                 ce[mode], stream))
+
+            if mode == "ce_pull":  # the pull ring reads the peers' own slots: stage them first
+                agg.device_view(slab.uc + rank * size, (size // 2,), torch.bfloat16).copy_(src)
+                torch.cuda.synchronize()
+                dist.barrier()
             for _ in range(2):  # warm-up
-                agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None, 0,
-                                             stream))
+                move()
             torch.cuda.synchronize()
             dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(reps):
-                agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), slab.mc + rank * size, size, None, 0,
-                                             stream))
+                move()
             e1.record()
             torch.cuda.synchronize()
             dist.barrier()

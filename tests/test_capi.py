@@ -66,6 +66,33 @@ def test_launch_rejects_bad_arguments_before_touching_the_gpu(pkg):
     assert b"scale" in L.agg_last_error()
 
 
+def test_reduce_scatter_layout_and_argument_checks(pkg):
+    agg = pkg.agg
+    L = pkg.lib()
+    assert L.agg_rs_args_size() == ctypes.sizeof(agg.agg_rs_args)
+    base = dict(X=0x1000, W=0x2000, Y=0x3000, part_uc=0x10000, part_mc=0x20000, cnt_uc=0x4000, cnt_mc=0x5000,
+                done_uc=0x6000, done_mc=0x7000, epoch=1, rank=0, world=2, M=512, N=256, K=256)
+
+    def launch(**kw):
+        a = agg.agg_rs_args()
+        for k, v in {**base, **kw}.items():
+            setattr(a, k, v)
+        return L.agg_launch_rs(ctypes.byref(a), None)
+
+    assert launch(world=1) == -1              # the twin needs 2..8 ranks
+    assert launch(world=9) == -1
+    assert launch(rank=2) == -1
+    assert launch(M=2 * 384) == -1            # row block not a multiple of 256
+    assert b"256" in L.agg_last_error()
+    assert launch(N=12) == -1
+    assert launch(K=12) == -1
+    assert launch(epoch=0) == -1
+    assert launch(Y=0x3008) == -1             # Y not 16-byte aligned
+    assert launch(cnt_mc=0) == -1
+    assert launch(M=2 * 256 * 64, N=256 * 129) == -1   # more tiles than counters
+    assert b"tiles" in L.agg_last_error()
+
+
 def test_errors_without_gpu_are_reported_not_raised(pkg):
     import torch
 

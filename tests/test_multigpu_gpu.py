@@ -104,12 +104,29 @@ def test_back_to_back_launches_with_new_inputs_p2():
         assert r["worst_rel_err"] <= 1e-2, r
 
 
-def test_multicast_sweep_p2_byte_identical():
+@pytest.mark.parametrize("mode", ["sm", "ce_mc", "ce_push", "ce_pull"])
+def test_multicast_sweep_p2_byte_identical(mode):
+    """The all-gather by multimem.st and by the copy engines
+    (vmm/test_vmm_multicast_speed.cu:172-254): every slot byte-identical on every GPU."""
     sizes = [1 << 20, 4 << 20, 16 << 20, 64 << 20]
-    res = run_ranks("multicast_sweep", 2, sizes=sizes)
+    res = run_ranks("multicast_sweep", 2, sizes=sizes, mode=mode)
     for r in res:
         for s in r["sweep"]:
             assert s["mismatched_words"] == 0, (r["rank"], s)
+
+
+@pytest.mark.parametrize("producer", ["ce_mc", "ce_push"])
+def test_copy_engine_producers_p2(producer):
+    """The fused kernel fed by copy engines instead of its producer warps:
+    chunk copies on an internal stream, arrival flags by cuStreamWriteValue32."""
+    res = run_ranks("ag_gemm_parity", 2, m_local=512, k=1024, n_r=512, launches=4, scheme="reference",
+                    producer=producer)
+    for r in res:
+        assert r["gather_ok"] and r["bad"] == 0 and r["launches_identical"], r
+        assert r["stats"]["max_rel_err"] <= 1e-2, r
+    res = run_ranks("ag_gemm_changing_inputs", 2, m_local=1024, k=2048, n_r=1024, launches=6, producer=producer)
+    for r in res:
+        assert r["worst_rel_err"] <= 1e-2, r
 
 
 def test_multimem_known_answers_p2():
@@ -118,6 +135,27 @@ def test_multimem_known_answers_p2():
         assert r["store_ok"] and r["red_ok"] and r["reduce_ok"], r
         assert r["ld_reduce_ok"] and r["red_v4_ok"], r
         assert r["barrier_status"] == 0 and r["barrier_flags_ok"], r
+
+
+@pytest.mark.parametrize("double_buffer", [True, False])
+def test_gemm_reduce_scatter_p2(double_buffer):
+    """The row-parallel twin: bf16 partial tiles in each slab, the owner's rows
+    summed through NVSwitch.  Ragged N and K; new activations every launch.
+    Tolerance: max rel err <= 1e-2, and per element the reference's check_close
+    (atol 0.1, rtol 0.02) widened by the bf16 rounding of each rank's partial
+    (2^-8 * sum of |partial|), the same rounding a bf16 NCCL reduce-scatter does."""
+    res = run_ranks("gemm_rs_parity", 2, m_per_rank=512, n=520, k=264, launches=3, double_buffer=double_buffer)
+    for r in res:
+        assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_gemm_reduce_scatter_wider(world):
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = run_ranks("gemm_rs_parity", world, m_per_rank=256, n=1024, k=512, launches=2)
+    for r in res:
+        assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
 
 
 @pytest.mark.parametrize("world", [4, 8])

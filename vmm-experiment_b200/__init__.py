@@ -4,4 +4,4 @@ The product is libagg.so (C ABI in include/agg.h, CUDA sources in csrc/);
 ``agg`` holds the Python host side (ctypes + torch.distributed plumbing).
 """
 from . import agg  # noqa: F401
-from .agg import AggError, AllGatherGemm, gemm, gemm_e4m3, lib, spmm_init  # noqa: F401
+from .agg import AggError, AllGatherGemm, GemmReduceScatter, gemm, gemm_e4m3, lib, spmm_init  # noqa: F401

@@ -35,7 +35,12 @@ AGG_FLAG_CHUNK_OFF = 0
 AGG_FLAG_DONE_OFF = 64 << 10
 AGG_FLAG_USER_OFF = 72 << 10
 AGG_ARGS_DOUBLE_BUFFER = 1
-ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain"}
+AGG_ARGS_CE_MC_PUSH = 2
+AGG_ARGS_CE_PEER_PUSH = 4
+AGG_CE_MC_PUSH, AGG_CE_PEER_PUSH, AGG_CE_PEER_PULL = 0, 1, 2
+PRODUCERS = {"sm": 0, "ce_mc": AGG_ARGS_CE_MC_PUSH, "ce_push": AGG_ARGS_CE_PEER_PUSH}
+ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain",
+              8: "reducer"}
 AGG_TRACE_SLOTS = 16
 TRACE_EVENTS = ["start", "prod_gate", "prod_done", "first_wait", "first_ready", "last_ready", "flag_wait_ns",
                 "loader_done", "mma_done", "epi_done", "end", "tiles", "mma_wait_ns", "mma_acc_ns", "load_wait_ns",
@@ -73,6 +78,7 @@ EXPORTS = [
     "agg_mc_broadcast", "agg_verify_bytes", "agg_verify_pattern_gather", "agg_alias_fence",
     "agg_multimem_ops_test", "agg_multimem_ld_reduce_v4", "agg_multimem_red_add_v4",
     "agg_mm_barrier", "agg_wait_flag", "agg_gemm_bf16_noalloc",
+    "agg_launch_rs", "agg_rs_args_size", "agg_ce_allgather", "agg_stream_write_u32",
 ]
 
 
@@ -122,6 +128,30 @@ class agg_args(ctypes.Structure):
     ]
 
 
+class agg_rs_args(ctypes.Structure):
+    _fields_ = [
+        ("X", ctypes.c_void_p),
+        ("W", ctypes.c_void_p),
+        ("Y", ctypes.c_void_p),
+        ("part_uc", ctypes.c_uint64),
+        ("part_mc", ctypes.c_uint64),
+        ("cnt_uc", ctypes.c_void_p),
+        ("cnt_mc", ctypes.c_void_p),
+        ("done_uc", ctypes.c_void_p),
+        ("done_mc", ctypes.c_void_p),
+        ("epoch", ctypes.c_uint32),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("M", ctypes.c_int32),
+        ("N", ctypes.c_int32),
+        ("K", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("status", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
+        ("trace", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -165,6 +195,10 @@ def lib() -> ctypes.CDLL:
         "agg_mm_barrier": ([vp, vp, i32, u32, i32, vp, u64, vp], i32),
         "agg_wait_flag": ([vp, u32, vp, u64, vp], i32),
         "agg_gemm_bf16_noalloc": ([vp, vp, vp, i32, i32, i32, i32, vp, vp], i32),
+        "agg_launch_rs": ([ctypes.POINTER(agg_rs_args), vp], i32),
+        "agg_rs_args_size": ([], sz),
+        "agg_ce_allgather": ([ctypes.POINTER(agg_rank_info), u64, vp, sz, i32, vp], i32),
+        "agg_stream_write_u32": ([u64, u32, vp], i32),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -374,10 +408,19 @@ class AllGatherGemm:
     """
 
     def __init__(self, m_local: int, k: int, *, dtype: str = "bf16", group=None, device=None,
-                 timeout_s: float = 10.0, host_group=None, double_buffer: bool = True):
+                 timeout_s: float = 10.0, host_group=None, double_buffer: bool = True, producer: str = "sm"):
+        """`producer` chooses who moves this rank's shard: "sm" (the kernel's own
+        warps, multimem.st; default), "ce_mc" (copy engines, one copy per chunk
+        into the multicast VA) or "ce_push" (copy engines, one copy per chunk and
+        peer); the copy-engine modes need bf16 and double buffering."""
         torch = _torch()
         import torch.distributed as dist
 
+        if producer not in PRODUCERS:
+            raise AggError(f"producer must be one of {sorted(PRODUCERS)}")
+        if producer != "sm" and (dtype != "bf16" or not double_buffer):
+            raise AggError("copy-engine producers need bf16 and double buffering")
+        self.producer = producer
         self.dtype = dtype
         self.elem = 1 if dtype == "e4m3" else 2
         self.m_local, self.k = m_local, k
@@ -463,7 +506,93 @@ class AllGatherGemm:
             a.done_mc = s.done(mc=True)
             if self.double_buffer:
                 a.flags |= AGG_ARGS_DOUBLE_BUFFER
+            a.flags |= PRODUCERS[self.producer]
         check(lib().agg_launch(ctypes.byref(a), _stream_ptr(stream)), "agg_launch")
+        return out
+
+    def check_status(self):
+        word = int(self.status.item())
+        if word:
+            raise AggError(f"device status: {describe_status(word)}")
+
+    def close(self):
+        if self.slab is not None:
+            self.slab.close()
+            self.slab = None
+
+
+class GemmReduceScatter:
+    """Y_r = rows [r*M/P, (r+1)*M/P) of sum_s X_s . W_s^T, fused in one kernel per rank.
+
+    The row-parallel twin of AllGatherGemm (a tensor-parallel down projection):
+    rank s holds X_s [M, K_s] and W_s [N, K_s], slices of the contraction.  Each
+    rank's kernel stores its bf16 partial product tile by tile into its
+    multicast slab; the owner of each row block reads the sum of all ranks'
+    tiles through NVSwitch (multimem.ld_reduce, fp32 adds) as they complete.
+    world == 1 runs the plain GEMM.  With `double_buffer` (default) the slab
+    holds two [M, N] partial regions used by launch parity.
+    """
+
+    def __init__(self, m: int, n: int, k_local: int, *, group=None, device=None, timeout_s: float = 10.0,
+                 host_group=None, double_buffer: bool = True):
+        torch = _torch()
+        import torch.distributed as dist
+
+        self.M, self.N, self.k = m, n, k_local
+        if dist.is_available() and dist.is_initialized():
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self.slab = None
+        self.double_buffer = double_buffer
+        if m % self.world or (self.world > 1 and (m // self.world) % 256):
+            raise AggError(f"M ({m}) must split into row blocks of a multiple of 256 over {self.world} ranks")
+        if self.world > 1:
+            hg = host_group if host_group is not None else dist.new_group(backend="gloo")
+            job = make_job_id(hg)
+            regions = 2 if double_buffer else 1
+            self.slab = MulticastSlab(self.rank, self.world, self.device.index, regions * m * n * 2, job,
+                                      _default_group_barrier(hg))
+
+    @property
+    def m_local(self) -> int:
+        return self.M // self.world
+
+    def new_trace(self):
+        torch = _torch()
+        return torch.zeros((lib().agg_num_sms(), AGG_TRACE_SLOTS), dtype=torch.int64, device=self.device)
+
+    def __call__(self, X_r, W_r, out=None, stream=None, trace=None):
+        torch = _torch()
+        if tuple(X_r.shape) != (self.M, self.k) or tuple(W_r.shape) != (self.N, self.k):
+            raise AggError(f"X_r must be [{self.M}, {self.k}] and W_r [{self.N}, {self.k}]")
+        _check_operand(X_r, "X_r", torch.bfloat16)
+        _check_operand(W_r, "W_r", torch.bfloat16)
+        if out is None:
+            out = torch.empty((self.m_local, self.N), dtype=torch.bfloat16, device=self.device)
+        if self.world == 1:
+            return gemm(X_r, W_r, out=out, status=self.status, stream=stream)
+        self.epoch += 1
+        s = self.slab
+        a = agg_rs_args()
+        a.X, a.W, a.Y = X_r.data_ptr(), W_r.data_ptr(), out.data_ptr()
+        a.part_uc, a.part_mc = s.uc, s.mc
+        a.cnt_uc, a.cnt_mc = s.flags(), s.flags(mc=True)
+        a.done_uc, a.done_mc = s.done(), s.done(mc=True)
+        a.epoch = self.epoch
+        a.rank, a.world = self.rank, self.world
+        a.M, a.N, a.K = self.M, self.N, self.k
+        a.flags = AGG_ARGS_DOUBLE_BUFFER if self.double_buffer else 0
+        a.status = self.status.data_ptr()
+        a.timeout_ns = self.timeout_ns
+        if trace is not None:
+            a.trace = trace.data_ptr()
+        check(lib().agg_launch_rs(ctypes.byref(a), _stream_ptr(stream)), "agg_launch_rs")
         return out
 
     def check_status(self):

@@ -117,6 +117,11 @@ struct alignas(64) KParams {
     int raster_n;  // 1: group n-tiles instead of m-tiles
     int dtype;
     int tile_m;  // rows per m-tile: 128 (one CTA) or 256 (a CTA pair)
+    // reduce-scatter twin (flags_* are then the per-tile counters of this launch's parity)
+    const uint8_t* part_mc;  // this launch's partial region [M, N] bf16, multicast VA
+    __nv_bfloat16* y;        // this rank's rows of the sum [M/world, N]
+    uint32_t rs_target;      // a tile's partials are all stored when its counter reaches this
+    int ext_producer;        // 1: copy engines move the shard (AGG_ARGS_CE_*), no producer warps
 };
 
 // Position `pos` of the m-tile visiting order -> global m-tile index.
@@ -158,6 +163,21 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& mt, in
     const int gs = min(p.group_m, p.num_m_tiles - first);
     nt = j / gs;
     mt = m_tile_at(p, first + (j - nt * gs));
+}
+
+// Reduce-scatter tile order, the same on every rank: m-major groups of
+// `group_m` m positions as above, where position pos is local m-tile pos / P
+// of owner pos % P, so that every owner's tiles complete at an even rate on all
+// ranks at once and its reducers always have finished tiles to work on.
+__device__ __forceinline__ void rs_tile_coords(const KParams& p, int t, int& mt, int& nt) {
+    const int per_group = p.group_m * p.num_n_tiles;
+    const int g = t / per_group;
+    const int j = t - g * per_group;
+    const int first = g * p.group_m;
+    const int gs = min(p.group_m, p.num_m_tiles - first);
+    nt = j / gs;
+    const int pos = first + (j - nt * gs);
+    mt = (pos % p.world) * (p.m_local / 256) + pos / p.world;
 }
 
 // ---- optional event trace (one row of AGG_TRACE_SLOTS u64 per CTA)
@@ -472,6 +492,7 @@ __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, u
 }
 
 __device__ __forceinline__ void role_producer(const KParams& p, int pw, const Deadline& dl) {
+    if (p.ext_producer) return;  // the copy engines move the shard and raise the flags
     const uint32_t lane = lane_id();
     int ok = 1;
     if (p.gate_done > 0) {
@@ -547,6 +568,69 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
                 atomicExch(p.chunk_cnt + c, 0u);  // ready for the next launch
                 fence_acq_rel_sys();
                 mm_red_add_release_u32(p.flags_mc + p.rank * AGG_MAX_CHUNKS + c, 1u);
+            }
+        }
+        if (failed(p.status)) break;
+    }
+    if (p.trace && lane == 0) trace_max(p, AGG_TR_PROD_DONE, globaltimer_ns());
+}
+
+// Reduce-scatter: this rank owns m-tiles [rank*L, (rank+1)*L).  Its reducer
+// warps take 32-row slices of its tiles by ticket, in the order the tiles
+// complete (rs_tile_coords restricted to this owner), wait until all ranks'
+// partials of the tile are stored (its counter reaches rs_target), and read
+// their sum through the multicast address: NVSwitch fetches every GPU's copy
+// and adds them (fp32), one 16-byte multimem.ld_reduce per lane and row.
+__device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& dl) {
+    const uint32_t lane = lane_id();
+    const int L = p.m_local / 256;
+    const int nN = p.num_n_tiles;
+    const int P = p.world;
+    const unsigned long long units = static_cast<unsigned long long>(L) * nN * 8ull;
+    for (;;) {
+        unsigned long long ticket = 0;
+        if (lane == 0) ticket = atomicAdd(p.ticket, 1ull);
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket >= units) break;
+        const int slice = static_cast<int>(ticket & 7ull);
+        int k = static_cast<int>(ticket >> 3);
+        // k-th owned tile in completion order: walk the m-position groups.
+        int pos = -1, nt = 0;
+        for (int first = 0; first < p.num_m_tiles; first += p.group_m) {
+            const int gs = min(p.group_m, p.num_m_tiles - first);
+            const int f_own = first + ((p.rank - first) % P + P) % P;  // first owned position >= first
+            const int owned = f_own < first + gs ? (first + gs - 1 - f_own) / P + 1 : 0;
+            if (k < owned * nN) {
+                nt = k / owned;
+                pos = f_own + (k - nt * owned) * P;
+                break;
+            }
+            k -= owned * nN;
+        }
+        if (pos < 0) break;  // not reached: units counts exactly the owned tiles
+        const int mt = p.rank * L + pos / P;
+        int ok = 1;
+        if (lane == 0) ok = wait_flag_geq(p.flags_uc + mt * nN + nt, p.rs_target, dl) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_REDUCE, static_cast<uint32_t>(mt * nN + nt));
+            break;
+        }
+        __syncwarp();
+        fence_proxy_alias();
+        const int col = nt * 256 + static_cast<int>(lane) * 8;
+        if (col < p.N) {
+            const int row0 = mt * 256 + slice * 32;
+            const uint8_t* src = p.part_mc + (static_cast<size_t>(row0) * p.N + col) * 2;
+            __nv_bfloat16* dst = p.y + static_cast<size_t>(row0 - p.rank * p.m_local) * p.N + col;
+            const size_t pitch = static_cast<size_t>(p.N);
+#pragma unroll 1
+            for (int r = 0; r < 32; r += 8) {
+                uint4 v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = mm_ld_reduce_bf16x8(src + (r + i) * pitch * 2);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + (r + i) * pitch) = v[i];
             }
         }
         if (failed(p.status)) break;
@@ -669,13 +753,13 @@ struct PairCfg {
     static_assert(STAGES <= 32, "stage masks are 32-bit");
 };
 
-template <int BN2, int ST, int SUB>
+template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             uint32_t crank, const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
-    if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
+    if (!RS && p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
     const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
     const int cluster_id = static_cast<int>(blockIdx.x >> 1);
     const int num_clusters = static_cast<int>(gridDim.x >> 1);
@@ -686,12 +770,15 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
     FlagWaitLog log;
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
         int mt, nt;
-        tile_coords(p, t, mt, nt);
+        if constexpr (RS)
+            rs_tile_coords(p, t, mt, nt);
+        else
+            tile_coords(p, t, mt, nt);
         ++log.tiles;
         const int row = mt * G::TILE_M + static_cast<int>(crank) * 128;  // this CTA's first row of gathered A
         const CUtensorMap* tma = &p.tm_a_src;
         int a_row = row;
-        if (p.world > 1) {
+        if (!RS && p.world > 1) {
             const int src = row / p.m_local;
             if (src == p.rank) {
                 a_row = row - src * p.m_local;
@@ -808,7 +895,7 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     }
 }
 
-template <int BN2, int ST, int SUB>
+template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
                                               uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
@@ -821,9 +908,27 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
     int acc = 0;
     uint32_t acc_phase = 0;
     int buf = 0;
+    if constexpr (RS) {
+        // The partial region this launch writes was last read (through the
+        // multicast address, by every owner) two launches ago with double
+        // buffering, else by the previous launch: wait until every rank is done.
+        if (p.gate_done > 0) {
+            int ok = 1;
+            if (lane == 0) ok = wait_flag_geq(p.done_uc, p.gate_done, dl) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) record_failure(p.status, AGG_ROLE_PROD, 1u);
+                return;
+            }
+            fence_proxy_alias();
+        }
+    }
     for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
         int mt, nt;
-        tile_coords(p, t, mt, nt);
+        if constexpr (RS)
+            rs_tile_coords(p, t, mt, nt);
+        else
+            tile_coords(p, t, mt, nt);
         int got = 1;
         if (lane == 0) got = mbar_wait_sleepy(&tfull[acc], acc_phase, dl) ? 1 : 0;
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -909,6 +1014,20 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
                 }
             }
         }
+        if constexpr (RS) {
+            // This warp's 32-row slice of the partial tile is out: once its TMA
+            // stores have landed, count it on the tile's counter in every GPU
+            // (8 slices per tile and rank).
+            static_assert(G::STAGED_EPI, "reduce-scatter publishes TMA-stored slices");
+            if (lane == 0) {
+                bulk_wait_group<0>();
+                fence_proxy_async_global();
+                fence_proxy_alias();
+                fence_acq_rel_sys();
+                mm_red_add_release_u32(p.flags_mc + mt * p.num_n_tiles + nt, 1u);
+            }
+            __syncwarp();
+        }
         if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
@@ -921,7 +1040,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
     __syncwarp();
 }
 
-template <int BN2, int ST, int SUB>
+template <int BN2, int ST, int SUB, bool RS = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __grid_constant__ KParams p) {
     using G = PairCfg<BN2, ST, SUB>;
     extern __shared__ uint8_t smem_raw[];
@@ -967,14 +1086,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     if (warp == 0) {
-        if (lane == 0) pair_loader<BN2, ST, SUB>(p, smem, full, empty, crank, dl);
+        if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, crank, dl);
     } else if (warp == 1) {
         if (lane == 0 && crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
-        pair_epilogue<BN2, ST, SUB>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+        pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
     } else if (p.world > 1) {
-        role_producer(p, warp - 2 - EPI_WARPS, dl);
+        if constexpr (RS)
+            role_reducer(p, dl);
+        else
+            role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
 
     tc_fence_before();
@@ -1417,6 +1539,7 @@ constexpr int kNumPairKernels = 5;
 struct DevInfo {
     int sms = 0;
     PairKernel pair[kNumPairKernels];
+    PairKernel rs;  // the reduce-scatter instantiation (256 x 256, 3 x 2 k-blocks)
     int rc = AGG_OK;
     std::string err;
 };
@@ -1455,6 +1578,8 @@ int device_info(int dev, const DevInfo** out) {
         // accumulator): measured slower on the 70B shapes, so it is chosen only
         // when asked for (AGG_KERNEL=wide).
         d.pair[4] = wide_kernel_entry(1.40f);
+        d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 3, 2, true>),
+                          PairCfg<256, 3, 2>::SMEM, 256, 128, 3, 2, false, 1.0f, 0};
         auto setup = [&]() -> int {
             AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
             AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
@@ -1463,7 +1588,8 @@ int device_info(int dev, const DevInfo** out) {
                 int rc = max_pair_clusters(k.fn, k.smem, d.sms, &k.clusters);
                 if (rc) return rc;
             }
-            return AGG_OK;
+            AGG_RT(cudaFuncSetAttribute(d.rs.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, d.rs.smem));
+            return max_pair_clusters(d.rs.fn, d.rs.smem, d.sms, &d.rs.clusters);
         };
         d.rc = setup();
         if (d.rc) d.err = agg_last_error();
@@ -1473,6 +1599,28 @@ int device_info(int dev, const DevInfo** out) {
     return AGG_OK;
 }
 
+
+// One launch of a CTA-pair kernel: a persistent grid of as many pairs as fit
+// at once (never more than there are tiles).
+int launch_pair(const PairKernel& k, KParams& p, cudaStream_t stream) {
+    const int clusters = std::max(1, std::min(k.clusters, p.num_tiles));
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(k.smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* kargs[] = {&p};
+    AGG_RT(cudaLaunchKernelExC(&cfg, k.fn, kargs));
+    return AGG_OK;
+}
 
 }  // namespace
 
@@ -1497,6 +1645,18 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
         if (!a->A_local_buf || !a->A_mc || !a->A_copy_ready || !a->A_copy_ready_mc || !a->done_uc || !a->done_mc)
             return fail(AGG_EINVAL, "agg_launch: multicast buffers missing");
         if (a->A_copy_epoch < 1) return fail(AGG_EINVAL, "agg_launch: epoch must start at 1");
+    }
+    const uint32_t ce_mode = a->flags & (AGG_ARGS_CE_MC_PUSH | AGG_ARGS_CE_PEER_PUSH);
+    if (ce_mode && world > 1) {
+        if (ce_mode == (AGG_ARGS_CE_MC_PUSH | AGG_ARGS_CE_PEER_PUSH))
+            return fail(AGG_EINVAL, "agg_launch: choose one copy-engine mode");
+        if (!(a->flags & AGG_ARGS_DOUBLE_BUFFER) || f8)
+            return fail(AGG_EINVAL, "agg_launch: copy-engine producers need bf16 and AGG_ARGS_DOUBLE_BUFFER");
+        for (int s = 0; s < world; ++s)
+            if (!a->A_peer[s]) return fail(AGG_EINVAL, "agg_launch: copy-engine producers need A_peer[%d]", s);
+        const uint64_t ready = reinterpret_cast<uint64_t>(a->A_copy_ready);
+        if (ready < a->A_peer[a->dev_idx] || ready % 4)
+            return fail(AGG_EINVAL, "agg_launch: A_copy_ready must lie in this rank's slab (A_peer[rank])");
     }
     const void* a_src = a->A_src;
     if (!a_src) {
@@ -1639,29 +1799,110 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
             return fail(AGG_EINVAL, "agg_launch: shard pointers must be 16-byte aligned");
     }
 
-    if (!pk) {
-        const int grid = std::max(1, std::min(di->sms, p.num_tiles));
-        ag_gemm_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(p);
-        AGG_RT(cudaGetLastError());
-        return AGG_OK;
-    }
-    const int clusters = std::max(1, std::min(pk->clusters, p.num_tiles));
-    cudaLaunchConfig_t cfg;
-    std::memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
-    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = static_cast<size_t>(pk->smem);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    void* kargs[] = {&p};
-    AGG_RT(cudaLaunchKernelExC(&cfg, pk->fn, kargs));
-    return AGG_OK;
+    auto launch_kernel = [&]() -> int {
+        if (!pk) {
+            const int grid = std::max(1, std::min(di->sms, p.num_tiles));
+            ag_gemm_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, stream>>>(p);
+            AGG_RT(cudaGetLastError());
+            return AGG_OK;
+        }
+        return launch_pair(*pk, p, stream);
+    };
+    if (!(ce_mode && world > 1)) return launch_kernel();
+
+    // Copy-engine producers: the copies (internal stream) and the kernel (the
+    // caller's stream) run side by side; the launch completes on `stream` when
+    // both have.  The region being overwritten is free without a device-side
+    // gate: this rank's previous launch has completed (stream order), so every
+    // rank has delivered its previous-launch chunks, which its own copies
+    // started only after its launch before that -- the last reader of this
+    // parity's region -- had completed.
+    p.ext_producer = 1;
+    cudaStream_t ce = nullptr;
+    rc = ce_begin(stream, &ce);
+    if (rc) return rc;
+    rc = ce_push_shard(a, a_src, m_local, static_cast<size_t>(a->K) * elem, region_off, parity, p.flag_target,
+                       (ce_mode & AGG_ARGS_CE_MC_PUSH) != 0, ce);
+    if (rc == AGG_OK) rc = launch_kernel();
+    const int rc_end = ce_end(stream);
+    return rc ? rc : rc_end;
+}
+
+int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
+    if (!a) return fail(AGG_EINVAL, "agg_launch_rs: null args");
+    const int world = a->world;
+    if (world < 2 || world > AGG_MAX_RANKS) return fail(AGG_EINVAL, "agg_launch_rs: world %d (2..8)", world);
+    if (a->rank < 0 || a->rank >= world) return fail(AGG_EINVAL, "agg_launch_rs: rank %d", a->rank);
+    if (a->M <= 0 || a->N <= 0 || a->K <= 0) return fail(AGG_EINVAL, "agg_launch_rs: empty shape");
+    if (a->M % world) return fail(AGG_EINVAL, "agg_launch_rs: M=%d not divisible by world=%d", a->M, world);
+    const int m_local = a->M / world;
+    if (m_local % 256) return fail(AGG_EINVAL, "agg_launch_rs: M/world=%d must be a multiple of 256", m_local);
+    if (a->K % 8 || a->N % 8) return fail(AGG_EINVAL, "agg_launch_rs: N and K must be multiples of 8");
+    if (!a->X || !a->W || !a->Y) return fail(AGG_EINVAL, "agg_launch_rs: null X, W or Y");
+    if (reinterpret_cast<uintptr_t>(a->Y) % 16) return fail(AGG_EINVAL, "agg_launch_rs: Y must be 16-byte aligned");
+    if (!a->part_uc || !a->part_mc || !a->cnt_uc || !a->cnt_mc || !a->done_uc || !a->done_mc)
+        return fail(AGG_EINVAL, "agg_launch_rs: multicast buffers missing");
+    if (a->part_uc % 16 || a->part_mc % 16) return fail(AGG_EINVAL, "agg_launch_rs: partial region not 16-byte aligned");
+    if (a->epoch < 1) return fail(AGG_EINVAL, "agg_launch_rs: epoch must start at 1");
+    const int num_m_tiles = a->M / 256;
+    const int num_n_tiles = (a->N + 255) / 256;
+    if (static_cast<long long>(num_m_tiles) * num_n_tiles > AGG_RS_MAX_TILES)
+        return fail(AGG_EINVAL, "agg_launch_rs: %d x %d tiles exceed %d", num_m_tiles, num_n_tiles, AGG_RS_MAX_TILES);
+
+    int dev = 0;
+    AGG_RT(cudaGetDevice(&dev));
+    const DevInfo* di = nullptr;
+    int rc = device_info(dev, &di);
+    if (rc) return rc;
+    if (di->rs.clusters < 1) return fail(AGG_ECUDA, "agg_launch_rs: kernel cannot be resident");
+
+    KParams p;
+    std::memset(&p, 0, sizeof(p));
+    const bool dbl = (a->flags & AGG_ARGS_DOUBLE_BUFFER) != 0;
+    const uint32_t e = a->epoch;
+    const uint32_t parity = dbl ? (e & 1u) : 0u;
+    const size_t region = static_cast<size_t>(a->M) * a->N * 2;
+    const uint32_t kb_elems = BK_BYTES / 2;
+    rc = encode_2d(&p.tm_a_src, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->X, a->K, a->M, kb_elems, BM, "tensor map X");
+    if (rc) return rc;
+    rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->W, a->K, a->N, kb_elems, di->rs.b_box,
+                   "tensor map W");
+    if (rc) return rc;
+    rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   reinterpret_cast<const void*>(a->part_uc + parity * region), a->N, a->M, EPI_COLS, EPI_ROWS,
+                   "tensor map partials");
+    if (rc) return rc;
+    p.M = a->M;
+    p.N = a->N;
+    p.K = a->K;
+    p.rank = a->rank;
+    p.world = world;
+    p.m_local = m_local;
+    p.tile_m = 256;
+    p.num_m_tiles = num_m_tiles;
+    p.num_n_tiles = num_n_tiles;
+    p.num_tiles = num_m_tiles * num_n_tiles;
+    p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * 2 + BK_BYTES * di->rs.sub - 1) / (BK_BYTES * di->rs.sub));
+    p.group_m = std::max(1, env_int("AGG_GROUP_M", 12));
+    p.dtype = AGG_DTYPE_BF16;
+    p.status = a->status;
+    p.timeout_ns = a->timeout_ns;
+    p.trace = reinterpret_cast<unsigned long long*>(a->trace);
+    p.epoch = e;
+    p.flags_uc = a->cnt_uc + parity * AGG_RS_MAX_TILES;
+    p.flags_mc = a->cnt_mc + parity * AGG_RS_MAX_TILES;
+    // Every tile's counter grows by 8 slices x world ranks per launch of its parity set.
+    const uint32_t ordinal = dbl ? (e + 1u) >> 1 : e;
+    p.rs_target = 8u * static_cast<uint32_t>(world) * ordinal;
+    const uint32_t prior = dbl ? (e > 2u ? e - 2u : 0u) : e - 1u;
+    p.gate_done = prior * static_cast<uint32_t>(world);
+    p.done_uc = a->done_uc;
+    p.done_mc = a->done_mc;
+    p.cta_counter = a->done_uc + 16;                                    // +64 B
+    p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);  // +128 B
+    p.part_mc = reinterpret_cast<const uint8_t*>(a->part_mc + parity * region);
+    p.y = static_cast<__nv_bfloat16*>(a->Y);
+    return launch_pair(di->rs, p, stream);
 }
 
 }  // namespace agg
@@ -1709,6 +1950,12 @@ int agg_gemm_e4m3(const void* A, const void* B, void* C, const float* scale_a, c
     a.status = status;
     return agg::launch_ag_gemm(&a, static_cast<cudaStream_t>(stream));
 }
+
+int agg_launch_rs(const agg_rs_args* args, void* stream) {
+    return agg::launch_gemm_rs(args, static_cast<cudaStream_t>(stream));
+}
+
+size_t agg_rs_args_size(void) { return sizeof(agg_rs_args); }
 
 int agg_num_sms(void) {
     const int s = agg::current_sms(nullptr);

@@ -34,6 +34,7 @@ namespace agg {
     X(cuMulticastBindMem)               \
     X(cuMulticastUnbind)                \
     X(cuMulticastGetGranularity)        \
+    X(cuStreamWriteValue32)             \
     X(cuTensorMapEncodeTiled)
 
 struct DriverApi {
@@ -53,6 +54,15 @@ int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 // Helpers that turn CUDA failures into library error codes.
 int check_rt(cudaError_t e, const char* what);
 int check_drv(CUresult r, const char* what);
+
+// Copy-engine producers of the fused kernel (agg_ce.cu).  ce_begin orders the
+// device's internal stream after `caller` and holds the device's copy-engine
+// state until ce_end, which makes `caller` wait for the copies; call ce_end
+// after every successful ce_begin.
+int ce_begin(cudaStream_t caller, cudaStream_t* ce);
+int ce_end(cudaStream_t caller);
+int ce_push_shard(const agg_args* a, const void* src, int m_local, size_t row_bytes, uint64_t region_off,
+                  uint32_t parity, uint32_t target, bool multicast, cudaStream_t ce);
 
 }  // namespace agg
 

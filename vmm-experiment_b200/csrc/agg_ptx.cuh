@@ -219,6 +219,17 @@ __device__ __forceinline__ float4 mm_ld_reduce_add_v4_f32(const float* mc_addr) 
     return r;
 }
 
+// Sum over every GPU's copy of 8 bf16 values (16 bytes), added in fp32 and
+// rounded to bf16 once.
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc_addr) {
+    uint4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(mc_addr)
+                 : "memory");
+    return r;
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
