@@ -362,6 +362,11 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="multicast write bandwidth sweep (1 MiB .. --sweep-max) instead of the GEMM")
     ap.add_argument("--sweep-max", type=int, default=1 << 30)
+    ap.add_argument("--sweep-ce", action="store_true",
+                    help="add the copy-engine all-gathers (multicast push, push ring, pull ring) to the sweep")
+    ap.add_argument("--producer", default="sm", choices=["sm", "ce_mc", "ce_push"],
+                    help="who moves the shards in the fused kernel: its producer warps (multimem.st) or the "
+                         "copy engines")
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
     ap.add_argument("--op", default="ag", choices=["ag", "rs"],
@@ -419,7 +424,8 @@ def main():
         slab = pkg.agg.MulticastSlab(rank, world, local_rank, world * sizes[-1], pkg.agg.make_job_id(host_group),
                                      lambda: dist.barrier(group=host_group))
         try:
-            rows = sweep.run(slab, sizes, reps=args.steps, warmup=args.warmup, group=host_group)
+            rows = sweep.run(slab, sizes, reps=args.steps, warmup=args.warmup, group=host_group,
+                             copy_engines=args.sweep_ce)
         finally:
             torch.cuda.synchronize()
             dist.barrier(group=host_group)
@@ -453,7 +459,7 @@ def main():
         A_in, B_in, S_a, S_b = A_r, B_r, None, None
     elem = 1 if f8 else 2
 
-    op = pkg.AllGatherGemm(m_local, K, dtype=args.dtype, host_group=host_group)
+    op = pkg.AllGatherGemm(m_local, K, dtype=args.dtype, host_group=host_group, producer=args.producer)
     stream = torch.cuda.current_stream()
 
     def launch(A, out, trace=None):

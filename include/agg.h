@@ -245,26 +245,28 @@ int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, i
 /* ---- the fused GEMM + reduce-scatter (row-parallel twin) ---------------------------- */
 /*
  * Y_r[M/P, N] = rows [r*M/P, (r+1)*M/P) of  sum_s X_s[M, K_s] . W_s[N, K_s]^T
- * (bf16 in, fp32 accumulate, bf16 partials, fp32 sum, bf16 out), in one kernel per
- * rank: the tensor-core warps compute every [256 x 256] tile of this rank's
- * partial product into its slab and raise the tile's counter on every GPU
- * (multimem.red); reducer warps on the owning rank pull the sum of all ranks'
- * copies of its tiles through NVSwitch (multimem.ld_reduce.add.acc::f32) as the
- * tiles complete.  The reduce-scatter channels that the reference's RankState
- * reserves (rs_calls, dmw_cnt[kDmwChannels]; include/multimem.cuh:13-17) have no
- * kernel in the reference; this is that path.
+ * (bf16 in, fp32 accumulate, bf16 partials, fp32 sum in source order, bf16 out),
+ * in one kernel per rank: the tensor-core warps compute every [256 x 256] tile of
+ * this rank's partial product and TMA-store it straight into the owning rank's
+ * inbox (slot r of its slab region, over NVLink for the other ranks), then raise
+ * the tile's counter on every GPU (multimem.red); reducer warps on the owner add
+ * the P slots of each of its tiles from local memory as the tiles complete.  The
+ * reduce-scatter channels that the reference's RankState reserves (rs_calls,
+ * dmw_cnt[kDmwChannels]; include/multimem.cuh:13-17) have no kernel in the
+ * reference; this is that path.
  * Shapes: M % P == 0, (M/P) % 256 == 0, N % 8 == 0, K % 8 == 0,
  * ceil(M/256) * ceil(N/256) <= AGG_RS_MAX_TILES.
- * Slab data: one [M, N] bf16 partial region (two with AGG_ARGS_DOUBLE_BUFFER,
- * region 1 right after region 0).  Counters and the done counter live in the
- * slab's flag area (AGG_FLAG_CHUNK_OFF, AGG_FLAG_DONE_OFF).
+ * Slab data: one inbox region of [P][M/P, N] bf16 (two with
+ * AGG_ARGS_DOUBLE_BUFFER, region 1 right after region 0) at the same offset in
+ * every rank's slab.  Counters and the done counter live in the slab's flag area
+ * (AGG_FLAG_CHUNK_OFF, AGG_FLAG_DONE_OFF).
  */
 typedef struct agg_rs_args {
     const void* X;        /* this rank's activation slice [M, K] bf16, K-major       */
     const void* W;        /* this rank's weight slice [N, K] bf16, K-major           */
     void* Y;              /* this rank's rows of the sum [M/world, N] bf16           */
-    uint64_t part_uc;     /* partial region 0, this GPU's unicast VA                  */
-    uint64_t part_mc;     /* partial region 0, multicast VA                           */
+    uint64_t part_peer[AGG_MAX_RANKS];  /* inbox region 0 in every rank's slab as     */
+                                        /* mapped here (part_peer[rank]: this GPU's)  */
     uint32_t* cnt_uc;     /* per-tile counters (flag area + AGG_FLAG_CHUNK_OFF), UC   */
     uint32_t* cnt_mc;     /* the same, multicast VA                                   */
     uint32_t* done_uc;    /* end-of-launch counter (flag area + AGG_FLAG_DONE_OFF), UC */

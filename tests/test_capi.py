@@ -70,13 +70,15 @@ def test_reduce_scatter_layout_and_argument_checks(pkg):
     agg = pkg.agg
     L = pkg.lib()
     assert L.agg_rs_args_size() == ctypes.sizeof(agg.agg_rs_args)
-    base = dict(X=0x1000, W=0x2000, Y=0x3000, part_uc=0x10000, part_mc=0x20000, cnt_uc=0x4000, cnt_mc=0x5000,
+    base = dict(X=0x1000, W=0x2000, Y=0x3000, cnt_uc=0x4000, cnt_mc=0x5000,
                 done_uc=0x6000, done_mc=0x7000, epoch=1, rank=0, world=2, M=512, N=256, K=256)
 
-    def launch(**kw):
+    def launch(peers=(0x10000, 0x20000), **kw):
         a = agg.agg_rs_args()
         for k, v in {**base, **kw}.items():
             setattr(a, k, v)
+        for i, v in enumerate(peers):
+            a.part_peer[i] = v
         return L.agg_launch_rs(ctypes.byref(a), None)
 
     assert launch(world=1) == -1              # the twin needs 2..8 ranks
@@ -89,6 +91,8 @@ def test_reduce_scatter_layout_and_argument_checks(pkg):
     assert launch(epoch=0) == -1
     assert launch(Y=0x3008) == -1             # Y not 16-byte aligned
     assert launch(cnt_mc=0) == -1
+    assert launch(peers=(0x10000, 0)) == -1   # a rank's inbox missing
+    assert launch(peers=(0x10000, 0x20008)) == -1
     assert launch(M=2 * 256 * 64, N=256 * 129) == -1   # more tiles than counters
     assert b"tiles" in L.agg_last_error()
 

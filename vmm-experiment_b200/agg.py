@@ -133,8 +133,7 @@ class agg_rs_args(ctypes.Structure):
         ("X", ctypes.c_void_p),
         ("W", ctypes.c_void_p),
         ("Y", ctypes.c_void_p),
-        ("part_uc", ctypes.c_uint64),
-        ("part_mc", ctypes.c_uint64),
+        ("part_peer", ctypes.c_uint64 * AGG_MAX_RANKS),
         ("cnt_uc", ctypes.c_void_p),
         ("cnt_mc", ctypes.c_void_p),
         ("done_uc", ctypes.c_void_p),
@@ -526,9 +525,9 @@ class GemmReduceScatter:
 
     The row-parallel twin of AllGatherGemm (a tensor-parallel down projection):
     rank s holds X_s [M, K_s] and W_s [N, K_s], slices of the contraction.  Each
-    rank's kernel stores its bf16 partial product tile by tile into its
-    multicast slab; the owner of each row block reads the sum of all ranks'
-    tiles through NVSwitch (multimem.ld_reduce, fp32 adds) as they complete.
+    rank's kernel stores its bf16 partial product tile by tile straight into
+    the owning rank's inbox (a slot per source rank in every slab); the owner
+    adds the slots of each of its tiles (fp32, source order) as they complete.
     world == 1 runs the plain GEMM.  With `double_buffer` (default) the slab
     holds two [M, N] partial regions used by launch parity.
     """
@@ -581,7 +580,8 @@ class GemmReduceScatter:
         s = self.slab
         a = agg_rs_args()
         a.X, a.W, a.Y = X_r.data_ptr(), W_r.data_ptr(), out.data_ptr()
-        a.part_uc, a.part_mc = s.uc, s.mc
+        for i in range(self.world):
+            a.part_peer[i] = s.peer_uc[i]
         a.cnt_uc, a.cnt_mc = s.flags(), s.flags(mc=True)
         a.done_uc, a.done_mc = s.done(), s.done(mc=True)
         a.epoch = self.epoch

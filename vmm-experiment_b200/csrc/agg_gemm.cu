@@ -85,6 +85,7 @@ struct alignas(64) KParams {
     CUtensorMap tm_a_gath;  // gathered A [M, K] in this GPU's slab
     CUtensorMap tm_b;       // B_r [N, K]
     CUtensorMap tm_c;       // C_r [M, N] bf16
+    CUtensorMap tm_out[AGG_MAX_RANKS];  // reduce-scatter: slot `rank` of every owner's inbox [M/P, N]
     const uint4* a_src;     // shard, for the producers' loads
     uint4* a_mc;            // multicast VA of this rank's slot in gathered A
     unsigned long long shard_bytes;
@@ -118,7 +119,7 @@ struct alignas(64) KParams {
     int dtype;
     int tile_m;  // rows per m-tile: 128 (one CTA) or 256 (a CTA pair)
     // reduce-scatter twin (flags_* are then the per-tile counters of this launch's parity)
-    const uint8_t* part_mc;  // this launch's partial region [M, N] bf16, multicast VA
+    const uint8_t* inbox;    // this GPU's inbox of this launch: [P][M/P, N] bf16, slot s from rank s
     __nv_bfloat16* y;        // this rank's rows of the sum [M/world, N]
     uint32_t rs_target;      // a tile's partials are all stored when its counter reaches this
     int ext_producer;        // 1: copy engines move the shard (AGG_ARGS_CE_*), no producer warps
@@ -575,12 +576,15 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
     if (p.trace && lane == 0) trace_max(p, AGG_TR_PROD_DONE, globaltimer_ns());
 }
 
-// Reduce-scatter: this rank owns m-tiles [rank*L, (rank+1)*L).  Its reducer
-// warps take 32-row slices of its tiles by ticket, in the order the tiles
-// complete (rs_tile_coords restricted to this owner), wait until all ranks'
-// partials of the tile are stored (its counter reaches rs_target), and read
-// their sum through the multicast address: NVSwitch fetches every GPU's copy
-// and adds them (fp32), one 16-byte multimem.ld_reduce per lane and row.
+// Reduce-scatter: this rank owns m-tiles [rank*L, (rank+1)*L).  Every rank's
+// epilogue has TMA-stored its partial of each such tile into slot `its rank`
+// of this GPU's inbox.  The epilogue warps, once their own tiles are out, take
+// 32-row slices of the owned tiles by ticket, in the order the tiles complete
+// (rs_tile_coords restricted to this owner), wait until all ranks' slices are
+// stored (the tile's counter reaches rs_target), and add the P slots from
+// local memory in source order (fp32), one 16-byte load per lane, row and
+// slot.  (Pulling the sum through NVSwitch with multimem.ld_reduce instead
+// moved only ~100 GB/s and stalled the SMs.)
 __device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& dl) {
     const uint32_t lane = lane_id();
     const int L = p.m_local / 256;
@@ -610,7 +614,7 @@ __device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& d
         if (pos < 0) break;  // not reached: units counts exactly the owned tiles
         const int mt = p.rank * L + pos / P;
         int ok = 1;
-        if (lane == 0) ok = wait_flag_geq(p.flags_uc + mt * nN + nt, p.rs_target, dl) ? 1 : 0;
+        if (lane == 0) ok = wait_flag_geq_quiet(p.flags_uc + mt * nN + nt, p.rs_target, dl) ? 1 : 0;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_REDUCE, static_cast<uint32_t>(mt * nN + nt));
@@ -620,17 +624,40 @@ __device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& d
         fence_proxy_alias();
         const int col = nt * 256 + static_cast<int>(lane) * 8;
         if (col < p.N) {
-            const int row0 = mt * 256 + slice * 32;
-            const uint8_t* src = p.part_mc + (static_cast<size_t>(row0) * p.N + col) * 2;
-            __nv_bfloat16* dst = p.y + static_cast<size_t>(row0 - p.rank * p.m_local) * p.N + col;
+            // row lr of the owner's block, slot s: inbox + ((s * m_local + lr) * N + col) * 2
+            const int lr0 = (mt - p.rank * L) * 256 + slice * 32;
             const size_t pitch = static_cast<size_t>(p.N);
+            const size_t slot = static_cast<size_t>(p.m_local) * pitch;
+            const uint4* src = reinterpret_cast<const uint4*>(
+                reinterpret_cast<const __nv_bfloat16*>(p.inbox) + static_cast<size_t>(lr0) * pitch + col);
+            __nv_bfloat16* dst = p.y + static_cast<size_t>(lr0) * pitch + col;
+            constexpr int R = 8;  // rows per pass: R loads in flight per lane and slot
 #pragma unroll 1
-            for (int r = 0; r < 32; r += 8) {
-                uint4 v[8];
+            for (int r = 0; r < 32; r += R) {
+                float acc[R][8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = mm_ld_reduce_bf16x8(src + (r + i) * pitch * 2);
+                for (int i = 0; i < R; ++i)
 #pragma unroll
-                for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + (r + i) * pitch) = v[i];
+                    for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
+                for (int s = 0; s < P; ++s) {  // fixed source order: the sum does not depend on timing
+                    uint4 v[R];
+#pragma unroll
+                    for (int i = 0; i < R; ++i) v[i] = __ldcg(src + (s * slot + (r + i) * pitch) / 8);
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            acc[i][2 * e] += __uint_as_float(w[e] << 16);
+                            acc[i][2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < R; ++i)
+                    *reinterpret_cast<uint4*>(dst + (r + i) * pitch) =
+                        make_uint4(pack_bf16x2(acc[i][0], acc[i][1]), pack_bf16x2(acc[i][2], acc[i][3]),
+                                   pack_bf16x2(acc[i][4], acc[i][5]), pack_bf16x2(acc[i][6], acc[i][7]));
             }
         }
         if (failed(p.status)) break;
@@ -895,6 +922,15 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
     }
 }
 
+// Reduce-scatter: one warp's slice of tile `tile` has landed in the owner's
+// inbox (its TMA stores completed): order it before the count, then raise the
+// tile's counter on every GPU.
+__device__ __forceinline__ void rs_publish(const KParams& p, int tile) {
+    fence_proxy_async_global();
+    fence_acq_rel_sys();
+    mm_red_add_release_u32(p.flags_mc + tile, 1u);
+}
+
 template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
                                               uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
@@ -908,10 +944,11 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
     int acc = 0;
     uint32_t acc_phase = 0;
     int buf = 0;
+    int rs_pending = -1;  // reduce-scatter: the tile whose slice awaits its count
     if constexpr (RS) {
-        // The partial region this launch writes was last read (through the
-        // multicast address, by every owner) two launches ago with double
-        // buffering, else by the previous launch: wait until every rank is done.
+        // The inbox slots this launch writes were last read (by every owner's
+        // reducers) two launches ago with double buffering, else by the
+        // previous launch: wait until every rank is done.
         if (p.gate_done > 0) {
             int ok = 1;
             if (lane == 0) ok = wait_flag_geq(p.done_uc, p.gate_done, dl) ? 1 : 0;
@@ -996,7 +1033,14 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&p.tm_c, b, col0, row0);
+                    if constexpr (RS) {
+                        // into slot `rank` of the owner's inbox (over NVLink for the
+                        // other ranks), row within the owner's block
+                        const int owner = row0 / p.m_local;
+                        tma_store_2d(&p.tm_out[owner], b, col0, row0 - owner * p.m_local);
+                    } else {
+                        tma_store_2d(&p.tm_c, b, col0, row0);
+                    }
                     bulk_commit_group();
                 }
                 buf ^= 1;
@@ -1015,16 +1059,18 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
             }
         }
         if constexpr (RS) {
-            // This warp's 32-row slice of the partial tile is out: once its TMA
-            // stores have landed, count it on the tile's counter in every GPU
-            // (8 slices per tile and rank).
+            // This warp's 32-row slice of the partial tile is out.  It is counted
+            // (on the tile's counter in every GPU, 8 slices per tile and rank) once
+            // its TMA stores have landed, which the warp checks only after issuing
+            // the next tile's stores: the wait then leaves that tile's
+            // BN2/EPI_COLS store groups in flight.
             static_assert(G::STAGED_EPI, "reduce-scatter publishes TMA-stored slices");
             if (lane == 0) {
-                bulk_wait_group<0>();
-                fence_proxy_async_global();
-                fence_proxy_alias();
-                fence_acq_rel_sys();
-                mm_red_add_release_u32(p.flags_mc + mt * p.num_n_tiles + nt, 1u);
+                if (rs_pending >= 0) {
+                    bulk_wait_group<BN2 / EPI_COLS>();
+                    rs_publish(p, rs_pending);
+                }
+                rs_pending = mt * p.num_n_tiles + nt;
             }
             __syncwarp();
         }
@@ -1035,6 +1081,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
     }
     if (lane == 0) {
         bulk_wait_group<0>();
+        if (RS && rs_pending >= 0) rs_publish(p, rs_pending);
         if (p.trace) trace_max(p, AGG_TR_EPI_DONE, globaltimer_ns());
     }
     __syncwarp();
@@ -1092,11 +1139,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
         pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
-    } else if (p.world > 1) {
-        if constexpr (RS)
-            role_reducer(p, dl);
-        else
-            role_producer(p, warp - 2 - EPI_WARPS, dl);
+        // Reduce-scatter: once its own tiles are out, the warp turns to summing
+        // the owned tiles (reducing next to the epilogue slowed it down).
+        if constexpr (RS) role_reducer(p, dl);
+    } else if (!RS && p.world > 1) {
+        role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
 
     tc_fence_before();
@@ -1840,9 +1887,11 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     if (a->K % 8 || a->N % 8) return fail(AGG_EINVAL, "agg_launch_rs: N and K must be multiples of 8");
     if (!a->X || !a->W || !a->Y) return fail(AGG_EINVAL, "agg_launch_rs: null X, W or Y");
     if (reinterpret_cast<uintptr_t>(a->Y) % 16) return fail(AGG_EINVAL, "agg_launch_rs: Y must be 16-byte aligned");
-    if (!a->part_uc || !a->part_mc || !a->cnt_uc || !a->cnt_mc || !a->done_uc || !a->done_mc)
+    if (!a->cnt_uc || !a->cnt_mc || !a->done_uc || !a->done_mc)
         return fail(AGG_EINVAL, "agg_launch_rs: multicast buffers missing");
-    if (a->part_uc % 16 || a->part_mc % 16) return fail(AGG_EINVAL, "agg_launch_rs: partial region not 16-byte aligned");
+    for (int s = 0; s < world; ++s)
+        if (!a->part_peer[s] || a->part_peer[s] % 16)
+            return fail(AGG_EINVAL, "agg_launch_rs: inbox of rank %d missing or not 16-byte aligned", s);
     if (a->epoch < 1) return fail(AGG_EINVAL, "agg_launch_rs: epoch must start at 1");
     const int num_m_tiles = a->M / 256;
     const int num_n_tiles = (a->N + 255) / 256;
@@ -1868,10 +1917,14 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->W, a->K, a->N, kb_elems, di->rs.b_box,
                    "tensor map W");
     if (rc) return rc;
-    rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                   reinterpret_cast<const void*>(a->part_uc + parity * region), a->N, a->M, EPI_COLS, EPI_ROWS,
-                   "tensor map partials");
-    if (rc) return rc;
+    // Slot `rank` of owner s's inbox (in its slab, as mapped here): rows of s's block.
+    const size_t slot_bytes = static_cast<size_t>(m_local) * a->N * 2;
+    for (int s = 0; s < world; ++s) {
+        rc = encode_2d(&p.tm_out[s], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                       reinterpret_cast<const void*>(a->part_peer[s] + parity * region + a->rank * slot_bytes), a->N,
+                       m_local, EPI_COLS, EPI_ROWS, "tensor map inbox");
+        if (rc) return rc;
+    }
     p.M = a->M;
     p.N = a->N;
     p.K = a->K;
@@ -1900,7 +1953,7 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     p.done_mc = a->done_mc;
     p.cta_counter = a->done_uc + 16;                                    // +64 B
     p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);  // +128 B
-    p.part_mc = reinterpret_cast<const uint8_t*>(a->part_mc + parity * region);
+    p.inbox = reinterpret_cast<const uint8_t*>(a->part_peer[a->rank] + parity * region);
     p.y = static_cast<__nv_bfloat16*>(a->Y);
     return launch_pair(di->rs, p, stream);
 }

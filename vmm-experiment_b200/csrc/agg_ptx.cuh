@@ -155,6 +155,23 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t tar
     }
 }
 
+// The same for waits that may last long next to busy warps: poll with relaxed
+// loads and a longer sleep (a system-scope acquire per poll disturbs the SM's
+// other memory traffic), then acquire once.
+__device__ __forceinline__ bool wait_flag_geq_quiet(const uint32_t* flag, uint32_t target, const Deadline& dl) {
+    if (ld_acquire_sys(flag) >= target) return true;
+    for (uint32_t spin = 1;; ++spin) {
+        __nanosleep(500);
+        if (ld_relaxed_sys(flag) >= target) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            return true;
+        }
+        if ((spin & 15u) == 0u) {
+            if (globaltimer_ns() > dl.end_ns || failed(dl.status)) return false;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ proxy fences
 __device__ __forceinline__ void fence_proxy_alias() {
     asm volatile("fence.proxy.alias;" ::: "memory");
@@ -214,17 +231,6 @@ __device__ __forceinline__ float4 mm_ld_reduce_add_v4_f32(const float* mc_addr) 
     float4 r;
     asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
-                 : "l"(mc_addr)
-                 : "memory");
-    return r;
-}
-
-// Sum over every GPU's copy of 8 bf16 values (16 bytes), added in fp32 and
-// rounded to bf16 once.
-__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc_addr) {
-    uint4 r;
-    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(mc_addr)
                  : "memory");
     return r;

@@ -5,12 +5,16 @@ This is the SM-driven counterpart of the reference's copy-engine multicast
 cases (vmm/test_vmm_multicast_speed.cu:172-194 single and concurrent pushes,
 verified at :301-429): message sizes from 1 MiB to 1 GiB, P = 2/4/8.
 
-Two patterns per size:
+Patterns per size:
   single      rank 0 broadcasts `size` bytes into slot 0 (one writer, P copies);
   concurrent  every rank broadcasts its own `size` bytes into its slot at the
               same time — an all-gather through NVSwitch; each GPU receives
-              (P-1) * size bytes.
-Times are device time (CUDA events) per push, the max over ranks.
+              (P-1) * size bytes;
+  allgather_ce_mc / _ce_push / _ce_pull  (with copy_engines=True) the same
+              all-gather by the copy engines, as the reference measures it:
+              one cudaMemcpyAsync into the multicast VA, a push ring to the
+              peers' unicast mappings, a pull ring from them (agg_ce_allgather).
+Times are device time (CUDA events) per all-gather or push, the max over ranks.
 """
 from __future__ import annotations
 
@@ -24,7 +28,11 @@ def _src(torch, size, rank, device):
     return (torch.rand(size // 2, device=device, generator=g) * 2 - 1).bfloat16()
 
 
-def run(slab, sizes, reps=10, warmup=3, group=None):
+CE_MODES = {"allgather_ce_mc": agg.AGG_CE_MC_PUSH, "allgather_ce_push": agg.AGG_CE_PEER_PUSH,
+            "allgather_ce_pull": agg.AGG_CE_PEER_PULL}
+
+
+def run(slab, sizes, reps=10, warmup=3, group=None, copy_engines=False):
     """Runs the sweep on an initialised MulticastSlab (collective over `group`)."""
     import torch
     import torch.distributed as dist
@@ -49,15 +57,22 @@ def run(slab, sizes, reps=10, warmup=3, group=None):
             raise agg.AggError(f"slab too small for {size} bytes x {world}")
         src = _src(torch, size, rank, device)
         row = {"bytes": size}
-        for pattern in ("single", "concurrent"):
-            writer = pattern == "concurrent" or rank == 0
+        patterns = ["single", "concurrent"] + (list(CE_MODES) if copy_engines else [])
+        for pattern in patterns:
+            writer = pattern != "single" or rank == 0
             dst = slab.mc + (rank if pattern == "concurrent" else 0) * size
 
             def push():
-                agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), dst, size, None, 0, stream))
+                if pattern in CE_MODES:
+                    agg.check(L.agg_ce_allgather(ctypes.byref(slab.info), 0, ctypes.c_void_p(src.data_ptr()), size,
+                                                 CE_MODES[pattern], stream))
+                else:
+                    agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), dst, size, None, 0, stream))
 
             # clear every GPU's copy so stale data cannot pass the check
             agg.device_view(slab.uc, (world * size,), torch.uint8, device).zero_()
+            if pattern == "allgather_ce_pull":  # the pull ring reads the peers' own slots
+                agg.device_view(slab.uc + rank * size, (size // 2,), torch.bfloat16, device).copy_(src)
             torch.cuda.synchronize()
             barrier()
             if writer:
@@ -76,14 +91,14 @@ def run(slab, sizes, reps=10, warmup=3, group=None):
             ms = max_ranks(e0.elapsed_time(e1) / reps if writer else 0.0)
             agg.check(L.agg_alias_fence(stream))
             bad.zero_()
-            slots = range(world) if pattern == "concurrent" else [0]
+            slots = [0] if pattern == "single" else range(world)
             for s in slots:
                 exp = _src(torch, size, s, device)
                 agg.check(L.agg_verify_bytes(ctypes.c_void_p(slab.uc + s * size), ctypes.c_void_p(exp.data_ptr()),
                                              size, ctypes.c_void_p(bad.data_ptr()), stream))
             torch.cuda.synchronize()
             mism = int(max_ranks(float(bad.item())))
-            recv = (world - 1) * size if pattern == "concurrent" else size
+            recv = size if pattern == "single" else (world - 1) * size
             row[pattern] = {"ms": ms, "sender_gbs": size / (ms * 1e-3) / 1e9,
                             "ingress_gbs_per_gpu": recv / (ms * 1e-3) / 1e9,
                             "delivered_gbs": (world * size if pattern == "single" else world * (world - 1) * size)
