@@ -223,6 +223,45 @@ def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=
         _teardown(op)
 
 
+def torch_ops_mlp(rank, world, port, m, k, n):
+    """A tensor-parallel MLP (up: ColumnParallelLinear, down: RowParallelLinear)
+    through the torch.library operators, against direct calls of the same kernels
+    (bit-identical) and the up projection against torch on gathered inputs."""
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    pkg = _init(rank, world, port)
+    ops = importlib.import_module(pkg.__name__ + ".torch_ops")
+    up = down = ref_ag = ref_rs = None
+    try:
+        m_local, n_r = m // world, n // world
+        g = torch.Generator(device="cuda").manual_seed(77 + rank)
+        x_r = torch.randn(m_local, k, device="cuda", generator=g).bfloat16()
+        w_up = (torch.randn(n_r, k, device="cuda", generator=g) * 0.05).bfloat16()
+        w_down = (torch.randn(k, n_r, device="cuda", generator=g) * 0.05).bfloat16()
+        up = ops.ColumnParallelLinear(w_up, m_local, host_group=dist.group.WORLD)
+        down = ops.RowParallelLinear(w_down, m, host_group=dist.group.WORLD)
+        h = up(x_r)       # [M, N/P]
+        y_r = down(h)     # [M/P, K]
+        ref_ag = pkg.AllGatherGemm(m_local, k, host_group=dist.group.WORLD)
+        ref_rs = pkg.GemmReduceScatter(m, k, n_r, host_group=dist.group.WORLD)
+        h2 = ref_ag(x_r, w_up)
+        y2 = ref_rs(h2, w_down)
+        torch.cuda.synchronize()
+        up.op.check_status()
+        down.op.check_status()
+        parts = [torch.empty_like(x_r).cpu() for _ in range(world)]
+        dist.all_gather(parts, x_r.cpu())
+        ref = torch.cat(parts).cuda().float() @ w_up.float().t()
+        up_err = float(((h.float() - ref).abs().max() / ref.abs().max()).item())
+        return {"rank": rank, "up_identical": bool(torch.equal(h, h2)), "down_identical": bool(torch.equal(y_r, y2)),
+                "up_rel_err": up_err, "shape_ok": tuple(y_r.shape) == (m_local, k)}
+    finally:
+        _teardown(up, down, ref_ag, ref_rs)
+
+
 def multicast_sweep(rank, world, port, sizes, reps=1, mode="sm"):
     """Each rank moves `size` bytes into its slot on every GPU -- mode "sm":
     multimem.st (agg_mc_broadcast); "ce_mc" / "ce_push" / "ce_pull": the copy

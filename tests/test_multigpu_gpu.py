@@ -149,6 +149,14 @@ def test_gemm_reduce_scatter_p2(double_buffer):
         assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
 
 
+def test_torch_ops_mlp_p2():
+    """ColumnParallelLinear -> RowParallelLinear through torch.ops.vmm_agg."""
+    res = run_ranks("torch_ops_mlp", 2, m=1024, k=1024, n=1536)
+    for r in res:
+        assert r["up_identical"] and r["down_identical"] and r["shape_ok"], r
+        assert r["up_rel_err"] <= 1e-2, r
+
+
 @pytest.mark.parametrize("world", [4, 8])
 def test_gemm_reduce_scatter_wider(world):
     if n_gpus() < world:
