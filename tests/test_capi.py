@@ -64,6 +64,15 @@ def test_launch_rejects_bad_arguments_before_touching_the_gpu(pkg):
     assert launch(dtype=7) == -1
     assert launch(dtype=1) == -1              # e4m3 without scales
     assert b"scale" in L.agg_last_error()
+    # copy-engine producers: one mode, double buffering, bf16, every rank's slab
+    mc = dict(world=2, M=512, A_mc=0x100000, A_local_buf=0x200000, A_copy_ready=0x300000, A_copy_ready_mc=0x400000,
+              done_uc=0x500000, done_mc=0x600000)
+    both = agg.AGG_ARGS_CE_MC_PUSH | agg.AGG_ARGS_CE_PEER_PUSH
+    assert launch(flags=both | agg.AGG_ARGS_DOUBLE_BUFFER, **mc) == -1
+    assert launch(flags=agg.AGG_ARGS_CE_MC_PUSH, **mc) == -1               # single buffer
+    assert b"DOUBLE_BUFFER" in L.agg_last_error()
+    assert launch(flags=agg.AGG_ARGS_CE_MC_PUSH | agg.AGG_ARGS_DOUBLE_BUFFER, **mc) == -1   # no A_peer
+    assert b"A_peer" in L.agg_last_error()
 
 
 def test_reduce_scatter_layout_and_argument_checks(pkg):

@@ -1785,9 +1785,11 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
     const size_t kblock_bytes = static_cast<size_t>(BK_BYTES) * (pk ? pk->sub : 1);
     p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + kblock_bytes - 1) / kblock_bytes);
-    // 12 m-tiles of 256 rows per group: measured on the 16384 x 57344 x 8192
-    // workload, DRAM reads fall from 24 GB (8) to 17 GB (10 to 14).
-    p.group_m = std::max(1, env_int("AGG_GROUP_M", pk ? 12 : 16));
+    // m-tiles of 256 rows per group.  One GPU: 12 (on the 16384 x 57344 x 8192
+    // workload DRAM reads fall from 24 GB with 8 to 17 GB with 10 to 14).  Across
+    // GPUs, where remote chunks are loaded from the slab as they arrive: 8
+    // (1.54-1.58 ms against 1.68-1.69 ms with 12 on that workload at P = 8).
+    p.group_m = std::max(1, env_int("AGG_GROUP_M", pk ? (world > 1 ? 8 : 12) : 16));
     p.raster_n = env_int("AGG_RASTER_N", 0) ? 1 : 0;
     p.dtype = a->dtype;
     p.scale_a = a->scale_a;
