@@ -519,7 +519,8 @@ def main():
     nvl_bytes = (world - 1) / world * M * K * elem if world > 1 else 0.0
     t_nvl = nvl_bytes / (NVLINK_GBS * 1e9)
     t_roof = max(t_tc, t_nvl)
-    traffic = ncu_traffic(args.workload)
+    # the committed DRAM capture is of the bf16 kernel at world 1
+    traffic = ncu_traffic(args.workload) if (not f8 and world == 1) else None
     roofline = {"bound": "tensor" if t_tc >= t_nvl else "nvlink", "achieved": achieved, "peak": peak_tc,
                 "unit": "TFLOP/s", "frac": t_roof / (kernel_ms * 1e-3),
                 "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)" + (" x 2 for e4m3" if f8 else ""),
