@@ -142,8 +142,15 @@ int launch_ag_gemm_warp_specialized(const ag_gemm_warp_specialized::fused_global
         std::fprintf(stderr, "launch_ag_gemm_warp_specialized: %s\n", agg_last_error());
         return rc;
     }
-    if (g.A_local_buf.raw_ptr && world > 1)
-        cudaMemcpyAsync(reinterpret_cast<void*>(g.A_local_buf.raw_ptr), a.A_local_buf,
-                        static_cast<size_t>(g.M) * K * sizeof(comm::bf16), cudaMemcpyDeviceToDevice, stream);
+    // The harness reads the gathered activation back from A_local_buf
+    // (vmm/main.cpp:302-309), but the kernel gathers it into the slab.  Copying
+    // it over costs one extra device pass of 2 * M * K bytes per launch (read +
+    // write; 117 MB at M = 4096, K = 7168): a caller that does not need the
+    // gathered rows passes a null A_local_buf, and one that passes the slab's
+    // own gathered region (rs.uc + gather_offset(...)) gets no copy either.
+    void* const dst = reinterpret_cast<void*>(g.A_local_buf.raw_ptr);
+    if (dst && dst != a.A_local_buf && world > 1)
+        cudaMemcpyAsync(dst, a.A_local_buf, static_cast<size_t>(g.M) * K * sizeof(comm::bf16),
+                        cudaMemcpyDeviceToDevice, stream);
     return AGG_OK;
 }

@@ -234,7 +234,9 @@ int agg_num_sms(void);
    and splits <= ceil(K/64); larger requests return AGG_EINVAL with the bytes
    they would need.  Same shape rules as agg_gemm_bf16, and A, B, C 16-byte aligned.
    The first call on a device looks up the array's device address (with that
-   device current); make that first call before any stream capture.  All calls
+   device current); make that first call before any stream capture.  The lookup
+   is redone, by the next call, whenever the device's current CUDA context is
+   not the one it was made in (after a cudaDeviceReset, for instance).  All calls
    on a device share the array and it keeps the last call's contents: each call
    first clears the counters it uses, so calls whose executions overlap on the
    GPU (concurrent streams) race and must be serialised by the caller. */

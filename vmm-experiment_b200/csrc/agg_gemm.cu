@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -123,7 +124,24 @@ struct alignas(64) KParams {
     __nv_bfloat16* y;        // this rank's rows of the sum [M/world, N]
     uint32_t rs_target;      // a tile's partials are all stored when its counter reaches this
     int ext_producer;        // 1: copy engines move the shard (AGG_ARGS_CE_*), no producer warps
+    // CTA-pair kernels: tiles are handed out in raster order from this launch's
+    // slot of g_sched (dynamic = 1), or round-robin by cluster (dynamic = 0).
+    int sched_slot;
+    int dynamic;
 };
+
+// Tile counters of the CTA-pair kernels' dynamic schedule.  Each launch takes
+// the next slot of a per-device ring (host side), counts its tiles out of
+// `next` and its finished CTAs into `done`; the last CTA to finish zeroes both,
+// so the slot is ready for its next launch.  Launches that run at the same
+// time (different streams) use different slots unless AGG_SCHED_SLOTS of them
+// are in flight at once.
+constexpr int AGG_SCHED_SLOTS = 1024;
+struct SchedSlot {
+    unsigned int next;
+    unsigned int done;
+};
+static __device__ SchedSlot g_sched[AGG_SCHED_SLOTS];
 
 // Position `pos` of the m-tile visiting order -> global m-tile index.
 __device__ __forceinline__ int m_tile_at(const KParams& p, int pos) {
@@ -756,6 +774,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
 //   even CTA    MMA issuer: waits `full`, issues the pair MMA, commits to
 //               `empty` in both CTAs, and to `tfull` in both CTAs per tile;
 //   both CTAs   epilogue: drains its own TMEM, arrives on the even CTA's `tempty`.
+// The pair's tile queue: the even CTA's loader takes each tile (from the
+// launch's counter, or round-robin) and publishes its index into a ring of
+// TQ_DEPTH slots in both CTAs' shared memory; the odd CTA's loader, the MMA
+// issuer and the eight epilogue warps read it from there.  -1 ends the launch.
+constexpr int TQ_DEPTH = 4;
+constexpr uint32_t TQ_READERS = 2 + 2 * EPI_WARPS;
+
+struct TileQueue {
+    int* ids;         // this CTA's ring
+    uint64_t* full;   // this CTA's, one arrival (from the even CTA's loader) per slot fill
+    uint64_t* empty;  // the even CTA's are used: TQ_READERS arrivals per slot drain
+    int pos;          // ring position of this role's next read or fill
+};
+
+// A reader's next tile: the id, -1 at the end, -2 when the wait gave up.
+__device__ __forceinline__ int tq_read(TileQueue& q, const Deadline& dl) {
+    const int s = q.pos % TQ_DEPTH;
+    const uint32_t ph = static_cast<uint32_t>(q.pos / TQ_DEPTH) & 1u;
+    ++q.pos;
+    if (!mbar_wait_cluster(&q.full[s], ph, dl)) return -2;
+    const int t = ld_shared_volatile_s32(&q.ids[s]);
+    mbar_arrive_cluster(mapa_shared(smem_u32(&q.empty[s]), 0));
+    return t;
+}
+
+// The even CTA's loader: take the next tile and publish it to both CTAs.
+__device__ __forceinline__ int tq_fill(const KParams& p, TileQueue& q, int& rr, const Deadline& dl) {
+    const int s = q.pos % TQ_DEPTH;
+    const uint32_t ph = static_cast<uint32_t>(q.pos / TQ_DEPTH) & 1u;
+    ++q.pos;
+    if (!mbar_wait_cluster(&q.empty[s], ph ^ 1u, dl)) return -2;
+    int t;
+    if (p.dynamic) {
+        const unsigned int n = atomicAdd(&g_sched[p.sched_slot].next, 1u);
+        t = n < static_cast<unsigned int>(p.num_tiles) ? static_cast<int>(n) : -1;
+    } else {
+        t = rr < p.num_tiles ? rr : -1;
+        rr += static_cast<int>(gridDim.x >> 1);
+    }
+    q.ids[s] = t;
+    st_shared_cluster_u32(mapa_shared(smem_u32(&q.ids[s]), 1), static_cast<uint32_t>(t));
+    mbar_arrive(&q.full[s]);
+    mbar_arrive_cluster(mapa_shared(smem_u32(&q.full[s]), 1));
+    return t;
+}
+
 template <int BN2, int ST, int SUB>
 struct PairCfg {
     static constexpr int TILE_M = 256;
@@ -771,9 +835,10 @@ struct PairCfg {
     // room; with one stage more it writes 16-byte row segments straight to HBM.
     static constexpr bool STAGED_EPI = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES + 256 + 1024 <= 232448;
     static constexpr int BAR_OFF = EPI_OFF + (STAGED_EPI ? EPI_WARPS * 2 * EPI_BUF_BYTES : 0);
-    static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1 + 2 * TQ_DEPTH;
     static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
-    static constexpr int SMEM = SLOT_OFF + 16 + 1024;
+    static constexpr int TQ_OFF = SLOT_OFF + 16;  // int tile ids [TQ_DEPTH]
+    static constexpr int SMEM = TQ_OFF + 4 * TQ_DEPTH + 1024;
     static constexpr uint32_t TMEM_COLS = 2 * BN2;  // two accumulators: 512 or 256 columns
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0 && A_BYTES % 1024 == 0, "swizzle alignment");
@@ -782,20 +847,25 @@ struct PairCfg {
 
 template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                                            uint32_t crank, const Deadline& dl) {
+                                            TileQueue& q, uint32_t crank, const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
     if (!RS && p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
     const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int rr = static_cast<int>(blockIdx.x >> 1);  // round-robin schedule: this pair's next tile
     int stage = 0;
     uint32_t phase = 0;
     uint32_t used = 0, last_par = 0;
     bool ok = true;
     FlagWaitLog log;
-    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+    while (ok) {
+        const int t = crank == 0 ? tq_fill(p, q, rr, dl) : tq_read(q, dl);
+        if (t == -2) {
+            record_failure(p.status, AGG_ROLE_TMA, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         int mt, nt;
         if constexpr (RS)
             rs_tile_coords(p, t, mt, nt);
@@ -858,19 +928,23 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
 template <int BN2, int ST, int SUB>
 __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
                                          uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
-                                         const Deadline& dl) {
+                                         TileQueue& q, const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
     const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, BN2) : make_idesc(1, 1, G::TILE_M, BN2);
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
-    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+    while (ok) {
+        const int t = tq_read(q, dl);
+        if (t == -2) {
+            record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         if (!mbar_wait_timed(&tempty[acc], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
             record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
             break;
@@ -933,14 +1007,13 @@ __device__ __forceinline__ void rs_publish(const KParams& p, int tile) {
 
 template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
-                                              uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
+                                              uint64_t* tempty, TileQueue& q, int warp, uint32_t crank,
+                                              const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
     const int eg = warp & 3;
     const uint32_t lane = lane_id();
     uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
     int acc = 0;
     uint32_t acc_phase = 0;
     int buf = 0;
@@ -960,7 +1033,15 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
             fence_proxy_alias();
         }
     }
-    for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+    for (;;) {
+        int t = 0;
+        if (lane == 0) t = tq_read(q, dl);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t == -2) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         int mt, nt;
         if constexpr (RS)
             rs_tile_coords(p, t, mt, nt);
@@ -1100,6 +1181,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::SLOT_OFF);
+    TileQueue q{reinterpret_cast<int*>(smem + G::TQ_OFF), drain + 1, drain + 1 + TQ_DEPTH, 0};
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
@@ -1119,6 +1201,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
             mbar_init(&tempty[a], 2 * EPI_WARPS);
         }
         mbar_init(drain, 1);
+        for (int s = 0; s < TQ_DEPTH; ++s) {
+            mbar_init(&q.full[s], 1);
+            mbar_init(&q.empty[s], TQ_READERS);
+        }
         fence_mbarrier_init();
         fence_proxy_async_smem();
     }
@@ -1133,12 +1219,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     if (warp == 0) {
-        if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, crank, dl);
+        if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, q, crank, dl);
     } else if (warp == 1) {
-        if (lane == 0 && crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        if (lane == 0 && crank == 0)
+            pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
-        pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+        pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
         // Reduce-scatter: once its own tiles are out, the warp turns to summing
         // the owned tiles (reducing next to the epilogue slowed it down).
         if constexpr (RS) role_reducer(p, dl);
@@ -1161,6 +1248,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         tmem_dealloc_pair(tmem_base, G::TMEM_COLS);
     }
     if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_END, globaltimer_ns());
+    if (p.dynamic && threadIdx.x == 0) {
+        // Every tile this CTA took was taken above (program order, then the
+        // fence): the last CTA to get here readies the slot for its next launch.
+        __threadfence();
+        SchedSlot& sl = g_sched[p.sched_slot];
+        if (atomicAdd(&sl.done, 1u) == gridDim.x - 1u) {
+            atomicExch(&sl.next, 0u);
+            atomicExch(&sl.done, 0u);
+        }
+    }
     if (p.world > 1 && threadIdx.x == 0) {
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
@@ -1191,29 +1288,35 @@ struct WideCfg {
     static constexpr int STAGES = 4;
     static constexpr int EPI_OFF = STAGES * STAGE;
     static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1;
+    static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1 + 2 * TQ_DEPTH;
     static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
-    static constexpr int SMEM = SLOT_OFF + 16 + 1024;
+    static constexpr int TQ_OFF = SLOT_OFF + 16;  // int tile ids [TQ_DEPTH]
+    static constexpr int SMEM = TQ_OFF + 4 * TQ_DEPTH + 1024;
     static constexpr uint32_t TMEM_COLS = 512;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0, "swizzle alignment");
 };
 
 __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                                            uint32_t crank, const Deadline& dl) {
+                                            TileQueue& q, uint32_t crank, const Deadline& dl) {
     using G = WideCfg;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
     if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
     const int kb_elems = p.dtype == AGG_DTYPE_BF16 ? BK_BYTES / 2 : BK_BYTES;
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
+    int rr = static_cast<int>(blockIdx.x >> 1);  // round-robin schedule: this pair's next tile
     int stage = 0;
     uint32_t phase = 0;
     uint32_t used = 0, last_par = 0;
     bool ok = true;
     FlagWaitLog log;
-    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+    while (ok) {
+        const int t = crank == 0 ? tq_fill(p, q, rr, dl) : tq_read(q, dl);
+        if (t == -2) {
+            record_failure(p.status, AGG_ROLE_TMA, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         int mt, nt;
         tile_coords(p, t, mt, nt);
         ++log.tiles;
@@ -1269,18 +1372,22 @@ __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uin
 
 __device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
                                          uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
-                                         const Deadline& dl) {
+                                         TileQueue& q, const Deadline& dl) {
     using G = WideCfg;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
     const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, 256) : make_idesc(1, 1, G::TILE_M, 256);
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
     int stage = 0;
     uint32_t phase = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
-    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+    while (ok) {
+        const int t = tq_read(q, dl);
+        if (t == -2) {
+            record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         for (int kb = 0; kb < p.num_kb; ++kb) {
             if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
                 record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
@@ -1337,17 +1444,24 @@ __device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32
 }
 
 __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
-                                              uint64_t* tempty, int warp, uint32_t crank, const Deadline& dl) {
+                                              uint64_t* tempty, TileQueue& q, int warp, uint32_t crank,
+                                              const Deadline& dl) {
     using G = WideCfg;
     const int eg = warp & 3;
     const uint32_t lane = lane_id();
     uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
-    const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-    const int num_clusters = static_cast<int>(gridDim.x >> 1);
     uint32_t acc_phase = 0;
     int buf = 0;
-    for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+    for (;;) {
+        int t = 0;
+        if (lane == 0) t = tq_read(q, dl);
+        t = __shfl_sync(0xffffffffu, t, 0);
+        if (t == -2) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, 0xFFFFFFu);
+            break;
+        }
+        if (t < 0) break;
         int mt, nt;
         tile_coords(p, t, mt, nt);
         int got = 1;
@@ -1442,6 +1556,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
     uint64_t* tempty = tfull + 1;  // [2]: one per N half
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::SLOT_OFF);
+    TileQueue q{reinterpret_cast<int*>(smem + G::TQ_OFF), drain + 1, drain + 1 + TQ_DEPTH, 0};
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
@@ -1460,6 +1575,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
         mbar_init(&tempty[0], 2 * EPI_WARPS);
         mbar_init(&tempty[1], 2 * EPI_WARPS);
         mbar_init(drain, 1);
+        for (int s = 0; s < TQ_DEPTH; ++s) {
+            mbar_init(&q.full[s], 1);
+            mbar_init(&q.empty[s], TQ_READERS);
+        }
         fence_mbarrier_init();
         fence_proxy_async_smem();
     }
@@ -1474,12 +1593,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     if (warp == 0) {
-        if (lane == 0) wide_loader(p, smem, full, empty, crank, dl);
+        if (lane == 0) wide_loader(p, smem, full, empty, q, crank, dl);
     } else if (warp == 1) {
-        if (lane == 0 && crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        if (lane == 0 && crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
-        wide_epilogue(p, smem, tmem_base, tfull, tempty, warp, crank, dl);
+        wide_epilogue(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
     } else if (p.world > 1) {
         role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
@@ -1497,6 +1616,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
         tmem_dealloc_pair(tmem_base, G::TMEM_COLS);
     }
     if (p.trace && threadIdx.x == 0) trace_set(p, AGG_TR_END, globaltimer_ns());
+    if (p.dynamic && threadIdx.x == 0) {
+        __threadfence();
+        SchedSlot& sl = g_sched[p.sched_slot];
+        if (atomicAdd(&sl.done, 1u) == gridDim.x - 1u) {
+            atomicExch(&sl.next, 0u);
+            atomicExch(&sl.done, 0u);
+        }
+    }
     if (p.world > 1 && threadIdx.x == 0) {
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
@@ -1649,8 +1776,15 @@ int device_info(int dev, const DevInfo** out) {
 
 // One launch of a CTA-pair kernel: a persistent grid of as many pairs as fit
 // at once (never more than there are tiles).
-int launch_pair(const PairKernel& k, KParams& p, cudaStream_t stream) {
+std::atomic<unsigned int> g_sched_seq[64];
+
+int launch_pair(const PairKernel& k, KParams& p, cudaStream_t stream, int dev) {
     const int clusters = std::max(1, std::min(k.clusters, p.num_tiles));
+    // Tile schedule: dynamic (tiles in raster order to whichever pair is free)
+    // unless AGG_SCHED=static asks for the round-robin one.
+    const char* sched = getenv("AGG_SCHED");
+    p.dynamic = (sched && std::strcmp(sched, "static") == 0) ? 0 : 1;
+    p.sched_slot = static_cast<int>(g_sched_seq[dev & 63].fetch_add(1u) % AGG_SCHED_SLOTS);
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
@@ -1855,7 +1989,7 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
             AGG_RT(cudaGetLastError());
             return AGG_OK;
         }
-        return launch_pair(*pk, p, stream);
+        return launch_pair(*pk, p, stream, dev);
     };
     if (!(ce_mode && world > 1)) return launch_kernel();
 
@@ -1957,7 +2091,7 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);  // +128 B
     p.inbox = reinterpret_cast<const uint8_t*>(a->part_peer[a->rank] + parity * region);
     p.y = static_cast<__nv_bfloat16*>(a->Y);
-    return launch_pair(di->rs, p, stream);
+    return launch_pair(di->rs, p, stream, dev);
 }
 
 }  // namespace agg

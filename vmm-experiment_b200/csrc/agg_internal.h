@@ -35,6 +35,8 @@ namespace agg {
     X(cuMulticastUnbind)                \
     X(cuMulticastGetGranularity)        \
     X(cuStreamWriteValue32)             \
+    X(cuCtxGetCurrent)                  \
+    X(cuCtxGetId)                       \
     X(cuTensorMapEncodeTiled)
 
 struct DriverApi {

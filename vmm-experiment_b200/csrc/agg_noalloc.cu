@@ -233,14 +233,19 @@ __device__ __forceinline__ void epilogue(const Params& p, uint32_t tmem_base, ui
             acc_phase ^= 1u;
         }
 
-        // Publish this quarter's partial; the splits-th arrival reduces it.
-        __threadfence();
+        // Publish this quarter's partial (every lane's stores, then one release
+        // fence and arrival); the splits-th arrival reduces it.
         __syncwarp();
+        __threadfence();
         uint32_t* cnt = p.counters + tile * 4 + q;
         uint32_t prev = 0;
-        if (lane == 0) prev = atomicAdd(cnt, 1u);
+        if (lane == 0) {
+            prev = atomicAdd(cnt, 1u);
+            __threadfence();  // lane 0 acquires the other splits' partials ...
+        }
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev != static_cast<uint32_t>(p.splits) - 1u) continue;
+        __syncwarp();        // ... and the warp barrier orders lanes 1-31 after lane 0
         __threadfence();
         const int mt = tile / p.num_n_tiles;
         const int nt = tile - mt * p.num_n_tiles;
@@ -334,34 +339,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) splitk_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------- host side
-// Per-device set-up, done once by the first call on each device with that
-// device current: the scratch's device address and the kernel's attributes.
+// Per-device set-up, redone whenever the device's current context differs
+// from the one it was done in (a cudaDeviceReset or a new primary context
+// reloads the module, which may move the scratch and drops the kernel's
+// shared-memory attribute): the scratch's device address, looked up with that
+// device current, and the kernel's attributes.  A failed set-up is not kept,
+// so the next call tries again.
 struct DevState {
-    int rc = AGG_OK;
-    std::string err;
+    unsigned long long ctx_id = 0;  // context the set-up was done in (0: none yet)
     unsigned char* scratch = nullptr;
     int sms = 0;
 };
 DevState g_state[64];
-std::once_flag g_once[64];
+std::mutex g_state_mu;
 
-int device_state(int dev, const DevState** out) {
+int device_state(int dev, DevState* out) {
     if (dev < 0 || dev >= 64) return fail(AGG_EINVAL, "device ordinal %d out of range", dev);
-    std::call_once(g_once[dev], [dev] {
-        DevState& d = g_state[dev];
-        auto setup = [&]() -> int {
-            void* ptr = nullptr;
-            AGG_RT(cudaGetSymbolAddress(&ptr, g_scratch));
-            d.scratch = static_cast<unsigned char*>(ptr);
-            AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
-            AGG_RT(cudaFuncSetAttribute(splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
-            return AGG_OK;
-        };
-        d.rc = setup();
-        if (d.rc) d.err = agg_last_error();
-    });
-    if (g_state[dev].rc) return fail(g_state[dev].rc, "no-alloc GEMM set-up failed: %s", g_state[dev].err.c_str());
-    *out = &g_state[dev];
+    const DriverApi& d = driver();
+    if (!d.ok) return fail(AGG_EDRIVER, "CUDA driver unavailable: %s", d.why.c_str());
+    CUcontext ctx = nullptr;
+    AGG_DRV(d.cuCtxGetCurrent(&ctx));
+    unsigned long long id = 0;
+    if (ctx) AGG_DRV(d.cuCtxGetId(ctx, &id));
+    std::lock_guard<std::mutex> lock(g_state_mu);
+    DevState& st = g_state[dev];
+    if (!ctx || st.ctx_id != id) {
+        // (With no context current yet, the runtime binds the device's primary
+        // context in the first call below.)
+        DevState fresh;
+        void* ptr = nullptr;
+        AGG_RT(cudaGetSymbolAddress(&ptr, g_scratch));
+        fresh.scratch = static_cast<unsigned char*>(ptr);
+        AGG_RT(cudaDeviceGetAttribute(&fresh.sms, cudaDevAttrMultiProcessorCount, dev));
+        AGG_RT(cudaFuncSetAttribute(splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
+        AGG_DRV(d.cuCtxGetCurrent(&ctx));
+        if (!ctx) return fail(AGG_ESTATE, "no CUDA context current on device %d", dev);
+        AGG_DRV(d.cuCtxGetId(ctx, &id));
+        fresh.ctx_id = id;
+        st = fresh;
+    }
+    *out = st;
     return AGG_OK;
 }
 
@@ -405,9 +422,10 @@ int launch(const void* A, const void* B, void* C, int M, int N, int K, int split
 
     int dev = 0;
     AGG_RT(cudaGetDevice(&dev));
-    const DevState* ds = nullptr;
-    int rc = device_state(dev, &ds);
+    DevState state;
+    int rc = device_state(dev, &state);
     if (rc) return rc;
+    const DevState* ds = &state;
 
     int s = splits;
     const int fit = static_cast<int>(MAX_UNITS / tiles);

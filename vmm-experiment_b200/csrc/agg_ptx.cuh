@@ -363,6 +363,43 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// try_wait with acquire at cluster scope: for phases completed by arrivals
+// (release.cluster) from the other CTA of the pair, so that what that CTA wrote
+// into this CTA's shared memory before arriving is visible after the wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const Deadline& dl) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait_cluster(a, parity)) return true;
+        if ((spin & 255u) == 0u) {
+            if (globaltimer_ns() > dl.end_ns || failed(dl.status)) return false;
+        }
+    }
+}
+
+// 32-bit store into the shared memory of any CTA of the cluster.
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_shared_volatile_s32(const int* p) {
+    int v;
+    asm volatile("ld.volatile.shared.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+
 // Arrive on an mbarrier of any CTA of the cluster (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");

@@ -15,12 +15,15 @@ Patterns per size:
               one cudaMemcpyAsync into the multicast VA, a push ring to the
               peers' unicast mappings, a pull ring from them (agg_ce_allgather).
 Times are device time (CUDA events) per all-gather or push, the max over ranks.
+Beside them, each rank's NVLink hardware counters (NVML, bytes sent and
+received over all links during the timed pushes) give the traffic on the wire.
 """
 from __future__ import annotations
 
 import ctypes
 
 from . import agg
+from .nvlink_counters import NvlinkCounters, delta
 
 
 def _src(torch, size, rank, device):
@@ -43,6 +46,12 @@ def run(slab, sizes, reps=10, warmup=3, group=None, copy_engines=False):
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     bad = torch.zeros(1, dtype=torch.int64, device=device)
     rows = []
+    counters = NvlinkCounters(device.index)
+
+    def per_rank(x):
+        out = [None] * world
+        dist.all_gather_object(out, x, group=group)
+        return out
 
     def barrier():
         dist.barrier(group=group)
@@ -81,14 +90,18 @@ def run(slab, sizes, reps=10, warmup=3, group=None, copy_engines=False):
             torch.cuda.synchronize()
             barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0 = counters.read()
             e0.record()
             if writer:
                 for _ in range(reps):
                     push()
             e1.record()
             torch.cuda.synchronize()
+            c1 = counters.read()
             barrier()
             ms = max_ranks(e0.elapsed_time(e1) / reps if writer else 0.0)
+            d = delta(c0, c1)
+            wire = per_rank(None if d is None else (d[0] / reps, d[1] / reps))
             agg.check(L.agg_alias_fence(stream))
             bad.zero_()
             slots = [0] if pattern == "single" else range(world)
@@ -104,6 +117,12 @@ def run(slab, sizes, reps=10, warmup=3, group=None, copy_engines=False):
                             "delivered_gbs": (world * size if pattern == "single" else world * (world - 1) * size)
                             / (ms * 1e-3) / 1e9,
                             "mismatched_words": mism}
+            if all(w is not None for w in wire):
+                # bytes on this GPU's links per push, and that over the max-over-ranks push time
+                row[pattern]["nvlink_counters"] = {
+                    "tx_bytes_per_push": [w[0] for w in wire], "rx_bytes_per_push": [w[1] for w in wire],
+                    "tx_gbs": [w[0] / (ms * 1e-3) / 1e9 for w in wire],
+                    "rx_gbs": [w[1] / (ms * 1e-3) / 1e9 for w in wire]}
         rows.append(row)
         del src
-    return rows
+    return rows, counters.describe()
