@@ -199,15 +199,75 @@ def ncu_traffic(workload):
     return float(m.group(1)) if m else None
 
 
+class NvmlClockSampler:
+    """Clock, power and clock-event-reason samples every 5 ms from NVML in a
+    background thread (reads only), so that even a timed region of a few tens of
+    milliseconds is covered by several samples."""
+
+    # nvmlClocksEventReason* bits
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index):
+        import threading
+
+        import pynvml
+        import torch
+
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(index).uuid)
+        self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        self.rows = []
+        self.stop_evt = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_evt.is_set():
+            try:
+                self.rows.append((float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)),
+                                  nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0,
+                                  int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))))
+            except nv.NVMLError:
+                pass
+            self.stop_evt.wait(0.005)
+
+    def start(self):
+        self.thread.start()
+        while not self.rows and self.thread.is_alive():
+            time.sleep(0.001)
+
+    def stop(self):
+        self.stop_evt.set()
+        self.thread.join(timeout=5)
+        if not self.rows:
+            return None
+        mhz = sorted(r[0] for r in self.rows)
+        watts = sorted(r[1] for r in self.rows)
+        reasons = sorted({name for r in self.rows for bit, name in self.REASONS.items() if r[2] & bit})
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "power_w": watts[len(watts) // 2], "samples": len(self.rows), "source": "NVML, 5 ms"}
+
+
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """Clock / throttle sampling during the timed region: NVML every 5 ms where
+    it answers, else nvidia-smi every 50 ms."""
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = None
+        try:
+            self.nvml = NvmlClockSampler(index)
+        except Exception:
+            self.nvml = None
 
     def start(self):
+        if self.nvml is not None:
+            self.nvml.start()
+            return
         fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
         os.close(fd)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -226,6 +286,8 @@ class ClockSampler:
             time.sleep(0.05)
 
     def stop(self):
+        if self.nvml is not None:
+            return self.nvml.stop()
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -247,7 +309,8 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": max_mhz, "reasons": reasons,
-                "power_w": watts[len(watts) // 2] if watts else None, "samples": len(rows)}
+                "power_w": watts[len(watts) // 2] if watts else None, "samples": len(rows),
+                "source": "nvidia-smi, 50 ms"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -298,6 +361,65 @@ def config_of(workload, world, dtype="bf16"):
             "M_per_rank": w["M"] // world, "P": world,
             "l2": "inputs larger than L2, no flush" if workload != "smoke" else "256 MiB L2 flush between steps",
             "parallelism": f"ag-tp{world}"}
+
+
+# ------------------------------------------------------------------ NVLink probe
+def run_nvlink_probe(args, emit):
+    """One process, GPUs 0 and 1 (the reference's thread-per-GPU set-up,
+    minfer_spmm_init, done here from one thread): GPU 0 broadcasts `size` bytes
+    once into the multicast slab with 16-byte multimem.st (agg_mc_broadcast),
+    then both GPUs' copies are checked byte for byte.  The broadcast waits on
+    nothing, so it can be profiled on its own (the NVLink tx/rx byte counters
+    of the sending GPU)."""
+    import ctypes
+
+    import torch
+
+    import __graft_entry__ as ge
+
+    pkg = ge.load_package()
+    agg = pkg.agg
+    L = agg.lib()
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("--nvlink-probe needs two GPUs")
+    size = args.nvlink_probe
+    world = 2
+    for r in range(world):
+        agg.spmm_init(r, world, r, world * size)
+    infos = [agg.spmm_init(r, world, r, world * size) for r in range(world)]
+    try:
+        torch.cuda.set_device(0)
+        g = torch.Generator(device="cuda:0").manual_seed(5)
+        src = (torch.rand(size // 2, device="cuda:0", generator=g) * 2 - 1).bfloat16()
+        stream = torch.cuda.current_stream(0)
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        agg.check(L.agg_mc_broadcast(ctypes.c_void_p(src.data_ptr()), infos[0].mc, size, None, 0, sp),
+                  "agg_mc_broadcast")
+        e1.record(stream)
+        torch.cuda.synchronize(0)
+        ms = e0.elapsed_time(e1)
+        bad = 0
+        for r in range(world):
+            with torch.cuda.device(r):
+                st = torch.cuda.current_stream(r)
+                rp = ctypes.c_void_p(st.cuda_stream)
+                exp = src.to(f"cuda:{r}")
+                cnt = torch.zeros(1, dtype=torch.int64, device=f"cuda:{r}")
+                agg.check(L.agg_alias_fence(rp))
+                agg.check(L.agg_verify_bytes(ctypes.c_void_p(infos[r].uc), ctypes.c_void_p(exp.data_ptr()), size,
+                                             ctypes.c_void_p(cnt.data_ptr()), rp))
+                torch.cuda.synchronize(r)
+                bad += int(cnt.item())
+    finally:
+        for r in range(world):
+            torch.cuda.synchronize(r)
+            L.agg_spmm_finalize(r)
+    emit({"probe": "multimem.st broadcast from GPU 0 to GPUs 0 and 1 (one launch)", "bytes": size, "ms": ms,
+          "sender_gbs": size / (ms * 1e-3) / 1e9, "mismatched_words": bad})
+    if bad:
+        sys.exit(1)
 
 
 # ------------------------------------------------------------------ our arm
@@ -520,6 +642,9 @@ def main():
                          "copy engines")
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
+    ap.add_argument("--nvlink-probe", type=int, default=0, metavar="BYTES",
+                    help="one process on GPUs 0-1: a single multicast broadcast of BYTES from GPU 0, checked on "
+                         "both GPUs (for a profiler capture of its NVLink counters)")
     ap.add_argument("--op", default="ag", choices=["ag", "rs"],
                     help="ag: the all-gather GEMM (default); rs: its GEMM + reduce-scatter twin "
                          "(default workload mlp70b_down)")
@@ -544,6 +669,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, emit)
+        return
+    if args.nvlink_probe:
+        run_nvlink_probe(args, emit)
         return
 
     import datetime

@@ -117,3 +117,21 @@ def test_errors_without_gpu_are_reported_not_raised(pkg):
     rc = L.agg_spmm_init(0, 2, 0, 1 << 20, ctypes.byref(info))
     assert rc < 0 and L.agg_last_error()
     assert L.agg_spmm_init(0, 2, 1, 1 << 20, ctypes.byref(info)) == -1  # rank != device
+
+
+def test_nvlink_counter_reader_degrades_without_nvml(pkg):
+    """The benchmark's NVLink byte counters come from NVML; where NVML or the
+    fields are missing, the reader says why and reads nothing (no exception)."""
+    import importlib
+
+    nv = importlib.import_module(pkg.__name__ + ".nvlink_counters")
+    c = nv.NvlinkCounters(0)
+    if c.available:  # a GPU host with NVLink: the counters only grow
+        a = c.read()
+        b = c.read()
+        assert b[0] >= a[0] and b[1] >= a[1]
+    else:
+        assert c.read() is None
+        assert "unavailable" in c.describe() and c.why
+    assert nv.delta(None, (1, 2)) is None
+    assert nv.delta((1, 2), (4, 7)) == (3, 5)

@@ -351,68 +351,91 @@ __device__ __forceinline__ void role_loader(const KParams& p, uint8_t* smem, uin
                 record_failure(p.status, AGG_ROLE_DRAIN, 1u);
 }
 
-__device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base,
-                                         uint64_t* full, uint64_t* empty, uint64_t* tfull,
-                                         uint64_t* tempty, uint64_t* drain, const Deadline& dl) {
-    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
-    const uint32_t idesc = f8 ? IDESC_E4M3 : IDESC_BF16;
-    const int k_steps = 4;                      // 128-byte k-block / 32 bytes per MMA
+// The whole warp runs the loop, one elected lane issues (see pair_mma_loop).
+template <bool F8>
+__device__ __forceinline__ void role_mma_loop(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                              uint64_t* empty, uint64_t* tfull, uint64_t* tempty,
+                                              const Deadline& dl) {
+    constexpr uint32_t IDESC = F8 ? IDESC_E4M3 : IDESC_BF16;
+    const uint32_t lane = lane_id();
+    const bool tr = p.trace != nullptr;
+    const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem + SMEM_STAGE_OFF));
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;
-    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
-    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait_timed(&tempty[acc], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
-            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        const unsigned long long ta = tr ? globaltimer_ns() : 0ull;
+        if (!mbar_wait_warp(&tempty[acc], acc_phase ^ 1u, dl)) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
             break;
         }
+        if (tr) acc_wait += globaltimer_ns() - ta;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
-                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
-                ok = false;
-                break;
+            if (!__all_sync(0xffffffffu, mbar_try_wait(smem_u32(&full[stage]), phase))) {
+                const unsigned long long t0 = tr ? globaltimer_ns() : 0ull;
+                ok = mbar_wait_warp(&full[stage], phase, dl);
+                if (tr) {
+                    full_wait += globaltimer_ns() - t0;
+                    ++full_waits;
+                }
+                if (!ok) {
+                    if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+                    break;
+                }
             }
             // (No tcgen05 fence here: the stage was filled by TMA and the mbarrier
             // wait already orders those async-proxy writes before the MMA reads.)
-            const uint32_t sa = smem_u32(smem + SMEM_STAGE_OFF + stage * STAGE_BYTES);
-            const uint64_t adesc = sw128_kmajor_desc(sa);
-            const uint64_t bdesc = sw128_kmajor_desc(sa + A_STAGE_BYTES);
+            const uint64_t adesc = desc0 + static_cast<uint64_t>((stage * STAGE_BYTES) >> 4);
+            const uint64_t bdesc = adesc + static_cast<uint64_t>(A_STAGE_BYTES >> 4);
 #pragma unroll
-            for (int k = 0; k < k_steps; ++k) {
+            for (int k = 0; k < 4; ++k) {
                 // +32 bytes along K inside the 128-byte swizzle row (>> 4 in the descriptor)
                 const uint64_t off = static_cast<uint64_t>(k * 2);
                 const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
-                if (f8)
-                    umma_f8(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                if constexpr (F8)
+                    umma_f8_warp(d_tmem, adesc + off, bdesc + off, IDESC, accumulate);
                 else
-                    umma_f16(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                    umma_f16_warp(d_tmem, adesc + off, bdesc + off, IDESC, accumulate);
             }
-            umma_commit(&empty[stage]);  // stage is free once these MMAs have read it
+            umma_commit_warp(&empty[stage]);  // stage is free once these MMAs have read it
             if (++stage == STAGES) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);  // accumulator complete
+        umma_commit_warp(&tfull[acc]);  // accumulator complete
         if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
         }
     }
-    // Every MMA this thread issued has finished once `drain` flips.
-    umma_commit(drain);
-    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
-    if (p.trace) {
-        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    if (tr && lane == 0) {
         trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
         trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
         trace_set(p, AGG_TR_MMA_STALLS, full_waits);
     }
+}
+
+__device__ __forceinline__ void role_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                         const Deadline& dl) {
+    if (p.dtype == AGG_DTYPE_E4M3)
+        role_mma_loop<true>(p, smem, tmem_base, full, empty, tfull, tempty, dl);
+    else
+        role_mma_loop<false>(p, smem, tmem_base, full, empty, tfull, tempty, dl);
+    // Every MMA this warp issued has finished once `drain` flips.
+    umma_commit_warp(drain);
+    if (lane_id() == 0) {
+        if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+        if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    }
+    __syncwarp();
 }
 
 __device__ __forceinline__ void role_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base,
@@ -728,7 +751,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
     if (warp == 0) {
         if (lane == 0) role_loader(p, smem, full, empty, dl);
     } else if (warp == 1) {
-        if (lane == 0) role_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
+        role_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
         role_epilogue(p, smem, tmem_base, tfull, tempty, warp, dl);
@@ -925,75 +948,107 @@ __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uin
                     record_failure(p.status, AGG_ROLE_DRAIN, 1u);
 }
 
-template <int BN2, int ST, int SUB>
-__device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
-                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
-                                         TileQueue& q, const Deadline& dl) {
+// The MMA issuer: the whole warp runs the loop (so descriptors stay in
+// uniform registers), one elected lane issues each tcgen05 instruction.
+template <int BN2, int ST, int SUB, bool F8>
+__device__ __forceinline__ void pair_mma_loop(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                              uint64_t* empty, uint64_t* tfull, uint64_t* tempty, TileQueue& q,
+                                              const Deadline& dl) {
     using G = PairCfg<BN2, ST, SUB>;
-    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
-    const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, BN2) : make_idesc(1, 1, G::TILE_M, BN2);
+    constexpr uint32_t IDESC = F8 ? make_idesc(0, 0, G::TILE_M, BN2) : make_idesc(1, 1, G::TILE_M, BN2);
+    const uint32_t lane = lane_id();
+    const bool tr = p.trace != nullptr;
+    const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;
-    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
-    while (ok) {
-        const int t = tq_read(q, dl);
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0;
+    for (;;) {
+        int t = 0;
+        if (lane == 0) t = tq_read(q, dl);
+        t = __shfl_sync(0xffffffffu, t, 0);
         if (t == -2) {
-            record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
+            if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
             break;
         }
         if (t < 0) break;
-        if (!mbar_wait_timed(&tempty[acc], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
-            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+        const unsigned long long ta = tr ? globaltimer_ns() : 0ull;
+        if (!mbar_wait_warp(&tempty[acc], acc_phase ^ 1u, dl)) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
             break;
         }
+        if (tr) acc_wait += globaltimer_ns() - ta;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
+        bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
-                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
-                ok = false;
+            if (!__all_sync(0xffffffffu, mbar_try_wait(smem_u32(&full[stage]), phase))) {
+                const unsigned long long t0 = tr ? globaltimer_ns() : 0ull;
+                ok = mbar_wait_warp(&full[stage], phase, dl);
+                if (tr) {
+                    full_wait += globaltimer_ns() - t0;
+                    ++full_waits;
+                }
+            }
+            if (!ok) {
+                if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
                 break;
             }
             // (No tcgen05 fence here: TMA filled the stage, the mbarrier orders it.)
-            const uint32_t sa = smem_u32(smem + stage * G::STAGE);
+            const uint64_t sdesc = desc0 + static_cast<uint64_t>((stage * G::STAGE) >> 4);
 #pragma unroll
             for (int u = 0; u < SUB; ++u) {
-                const uint64_t adesc = sw128_kmajor_desc(sa + u * G::A_SUB);
-                const uint64_t bdesc = sw128_kmajor_desc(sa + G::A_BYTES + u * G::B_SUB);
+                const uint64_t adesc = sdesc + static_cast<uint64_t>((u * G::A_SUB) >> 4);
+                const uint64_t bdesc = sdesc + static_cast<uint64_t>((G::A_BYTES + u * G::B_SUB) >> 4);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
+                    // +32 bytes along K inside the 128-byte swizzle row
                     const uint64_t off = static_cast<uint64_t>(k * 2);
                     const uint32_t accumulate = (kb > 0 || u > 0 || k > 0) ? 1u : 0u;
-                    if (f8)
-                        umma_f8_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                    if constexpr (F8)
+                        umma_f8_pair_warp(d_tmem, adesc + off, bdesc + off, IDESC, accumulate);
                     else
-                        umma_f16_pair(d_tmem, adesc + off, bdesc + off, idesc, accumulate);
+                        umma_f16_pair_warp(d_tmem, adesc + off, bdesc + off, IDESC, accumulate);
                 }
             }
-            umma_commit_pair_mc(&empty[stage], 0x3);
+            umma_commit_pair_mc_warp(&empty[stage], 0x3);
             if (++stage == G::STAGES) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
         if (!ok) break;
-        umma_commit_pair_mc(&tfull[acc], 0x3);
+        umma_commit_pair_mc_warp(&tfull[acc], 0x3);
         if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
         }
     }
-    umma_commit_pair_mc(drain, 0x1);
-    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
-    if (p.trace) {
-        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    if (tr && lane == 0) {
         trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
         trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
         trace_set(p, AGG_TR_MMA_STALLS, full_waits);
     }
+}
+
+template <int BN2, int ST, int SUB>
+__device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                         TileQueue& q, const Deadline& dl) {
+    if (p.dtype == AGG_DTYPE_E4M3)
+        pair_mma_loop<BN2, ST, SUB, true>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+    else
+        pair_mma_loop<BN2, ST, SUB, false>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+    // Every MMA issued has finished once `drain` flips.
+    umma_commit_pair_mc_warp(drain, 0x1);
+    int drained = 1;
+    if (lane_id() == 0) {
+        drained = mbar_wait_for(drain, 0, 500000000ull) ? 1 : 0;
+        if (!drained) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+        if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    }
+    __syncwarp();
 }
 
 // Reduce-scatter: one warp's slice of tile `tile` has landed in the owner's
@@ -1221,8 +1276,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     if (warp == 0) {
         if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, q, crank, dl);
     } else if (warp == 1) {
-        if (lane == 0 && crank == 0)
-            pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
+        if (crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
         pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
@@ -1370,34 +1424,43 @@ __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uin
                     record_failure(p.status, AGG_ROLE_DRAIN, 1u);
 }
 
-__device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
-                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
-                                         TileQueue& q, const Deadline& dl) {
+// The whole warp runs the loop, one elected lane issues (see pair_mma_loop).
+template <bool F8>
+__device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                              uint64_t* empty, uint64_t* tfull, uint64_t* tempty, TileQueue& q,
+                                              const Deadline& dl) {
     using G = WideCfg;
-    const bool f8 = p.dtype == AGG_DTYPE_E4M3;
-    const uint32_t idesc = f8 ? make_idesc(0, 0, G::TILE_M, 256) : make_idesc(1, 1, G::TILE_M, 256);
+    constexpr uint32_t IDESC = F8 ? make_idesc(0, 0, G::TILE_M, 256) : make_idesc(1, 1, G::TILE_M, 256);
+    const uint32_t lane = lane_id();
+    const bool tr = p.trace != nullptr;
+    const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
     int stage = 0;
     uint32_t phase = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;
-    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0, acc_waits = 0;
-    while (ok) {
-        const int t = tq_read(q, dl);
+    unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0;
+    for (;;) {
+        int t = 0;
+        if (lane == 0) t = tq_read(q, dl);
+        t = __shfl_sync(0xffffffffu, t, 0);
         if (t == -2) {
-            record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
+            if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
             break;
         }
         if (t < 0) break;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!mbar_wait_timed(&full[stage], phase, dl, p.trace != nullptr, full_wait, full_waits)) {
-                record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
-                ok = false;
-                break;
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb && ok; ++kb) {
+            if (!__all_sync(0xffffffffu, mbar_try_wait(smem_u32(&full[stage]), phase))) {
+                const unsigned long long t0 = tr ? globaltimer_ns() : 0ull;
+                ok = mbar_wait_warp(&full[stage], phase, dl);
+                if (tr) {
+                    full_wait += globaltimer_ns() - t0;
+                    ++full_waits;
+                }
+                if (!ok) break;
             }
-            const uint32_t sa = smem_u32(smem + stage * G::STAGE);
-            const uint64_t adesc = sw128_kmajor_desc(sa);
-            const uint64_t bdesc0 = sw128_kmajor_desc(sa + G::A_BYTES);
-            const uint64_t bdesc1 = sw128_kmajor_desc(sa + G::A_BYTES + G::B_HALF);
+            const uint64_t adesc = desc0 + static_cast<uint64_t>((stage * G::STAGE) >> 4);
+            const uint64_t bdesc0 = adesc + static_cast<uint64_t>(G::A_BYTES >> 4);
+            const uint64_t bdesc1 = bdesc0 + static_cast<uint64_t>(G::B_HALF >> 4);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint64_t off = static_cast<uint64_t>(k * 2);
@@ -1406,41 +1469,55 @@ __device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32
                 for (int h = 0; h < 2; ++h) {
                     if (kb == 0 && k == 0) {
                         // the epilogue must have read this half of the previous tile
-                        if (!mbar_wait_timed(&tempty[h], acc_phase ^ 1u, dl, p.trace != nullptr, acc_wait, acc_waits)) {
-                            record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
-                            ok = false;
-                            break;
-                        }
+                        const unsigned long long ta = tr ? globaltimer_ns() : 0ull;
+                        ok = mbar_wait_warp(&tempty[h], acc_phase ^ 1u, dl);
+                        if (tr) acc_wait += globaltimer_ns() - ta;
+                        if (!ok) break;
                         tc_fence_after();
                     }
                     const uint32_t d = tmem_base + static_cast<uint32_t>(h * 256);
                     const uint64_t bd = (h ? bdesc1 : bdesc0) + off;
-                    if (f8)
-                        umma_f8_pair(d, adesc + off, bd, idesc, accumulate);
+                    if constexpr (F8)
+                        umma_f8_pair_warp(d, adesc + off, bd, IDESC, accumulate);
                     else
-                        umma_f16_pair(d, adesc + off, bd, idesc, accumulate);
+                        umma_f16_pair_warp(d, adesc + off, bd, IDESC, accumulate);
                 }
                 if (!ok) break;
             }
             if (!ok) break;
-            umma_commit_pair_mc(&empty[stage], 0x3);
+            umma_commit_pair_mc_warp(&empty[stage], 0x3);
             if (++stage == G::STAGES) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
-        if (!ok) break;
-        umma_commit_pair_mc(tfull, 0x3);
+        if (!ok) {
+            if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, static_cast<uint32_t>(t));
+            break;
+        }
+        umma_commit_pair_mc_warp(tfull, 0x3);
         acc_phase ^= 1u;
     }
-    umma_commit_pair_mc(drain, 0x1);
-    if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
-    if (p.trace) {
-        trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    if (tr && lane == 0) {
         trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
         trace_set(p, AGG_TR_MMA_ACC_NS, acc_wait);
         trace_set(p, AGG_TR_MMA_STALLS, full_waits);
     }
+}
+
+__device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
+                                         uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                         TileQueue& q, const Deadline& dl) {
+    if (p.dtype == AGG_DTYPE_E4M3)
+        wide_mma_loop<true>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+    else
+        wide_mma_loop<false>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+    umma_commit_pair_mc_warp(drain, 0x1);
+    if (lane_id() == 0) {
+        if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
+        if (p.trace) trace_set(p, AGG_TR_MMA_DONE, globaltimer_ns());
+    }
+    __syncwarp();
 }
 
 __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
@@ -1595,7 +1672,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
     if (warp == 0) {
         if (lane == 0) wide_loader(p, smem, full, empty, q, crank, dl);
     } else if (warp == 1) {
-        if (lane == 0 && crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
+        if (crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
         wide_epilogue(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
@@ -1743,15 +1820,17 @@ int device_info(int dev, const DevInfo** out) {
     if (dev < 0 || dev >= 64) return fail(AGG_EINVAL, "device ordinal %d out of range", dev);
     std::call_once(g_dev_once[dev], [dev] {
         DevInfo& d = g_dev[dev];
-        // relative cost per output element, from sustained runs of each variant
+        // Relative cost per output element, from sustained (power-capped) runs
+        // of each variant on the 16384 x 57344 x 8192 and 16384 x 7168 x 8192
+        // GEMMs.  The wide 256 x 512 tile reads a quarter fewer operand bytes
+        // from L2 per FLOP, which the 1 kW cap turns into clock; its epilogue
+        // is partly exposed (one accumulator fills TMEM), and it still comes
+        // out ahead wherever its coarser waves do not cost more.
         d.pair[0] = pair_kernel_entry<256, 3, 2>(1.00f);
-        d.pair[1] = pair_kernel_entry<256, 6, 1>(1.08f);
-        d.pair[2] = pair_kernel_entry<128, 4, 2>(1.35f);
-        d.pair[3] = pair_kernel_entry<128, 8, 1>(1.45f);
-        // The wide tile reads 21% fewer L2 sectors but exposes its epilogue (one
-        // accumulator): measured slower on the 70B shapes, so it is chosen only
-        // when asked for (AGG_KERNEL=wide).
-        d.pair[4] = wide_kernel_entry(1.40f);
+        d.pair[1] = pair_kernel_entry<256, 6, 1>(1.02f);
+        d.pair[2] = pair_kernel_entry<128, 4, 2>(1.12f);
+        d.pair[3] = pair_kernel_entry<128, 8, 1>(1.15f);
+        d.pair[4] = wide_kernel_entry(0.93f);
         d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 3, 2, true>),
                           PairCfg<256, 3, 2>::SMEM, 256, 128, 3, 2, false, 1.0f, 0};
         auto setup = [&]() -> int {

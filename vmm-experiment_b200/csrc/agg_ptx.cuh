@@ -452,6 +452,89 @@ __device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t a_desc, u
         : "memory");
 }
 
+// Warp-wide forms for an issuing warp whose 32 lanes run the same loop: one
+// lane, picked by elect.sync inside the same asm block, issues the instruction.
+// Keeping the whole warp on the loop keeps its operands warp-uniform, so the
+// compiler can hold them in uniform registers instead of moving them there
+// before every tcgen05 instruction (which costs the single-lane form about a
+// hundred cycles per MMA).
+__device__ __forceinline__ void umma_f16_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                   uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f8_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f8_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_mc_warp(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+
+// mbarrier wait for a whole warp: every lane polls, the warp leaves together
+// (true), or together when lane 0 sees the deadline pass (false).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const Deadline& dl) {
+    const uint32_t a = smem_u32(bar);
+    if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
+    for (uint32_t spin = 1;; ++spin) {
+        if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
+        if ((spin & 255u) == 0u) {
+            int late = 0;
+            if ((threadIdx.x & 31u) == 0u) late = (globaltimer_ns() > dl.end_ns || failed(dl.status)) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, late, 0)) return false;
+        }
+    }
+}
+
 // Arrive on `bar` (same smem offset) in every CTA of `cta_mask` once all tcgen05
 // operations issued so far by this thread have completed.
 __device__ __forceinline__ void umma_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
