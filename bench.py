@@ -614,11 +614,8 @@ def run_rs(args, pkg, rank, world, dev, host_group, emit):
     op.close()
     if rank == 0:
         emit(out)
-    if world > 1:
-        barrier()
-        dist.destroy_process_group()
-    if not out["parity"]["ok"]:
-        sys.exit(1)
+    barrier()
+    return out["parity"]["ok"]
 
 
 def main():
@@ -642,6 +639,9 @@ def main():
                          "copy engines")
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
+    ap.add_argument("--also", default="", metavar="RUNS",
+                    help="comma-separated further runs in the same process group after the first, each "
+                         "WORKLOAD[:e4m3][:ce_mc|ce_push] or rs[:WORKLOAD]; one result line each")
     ap.add_argument("--nvlink-probe", type=int, default=0, metavar="BYTES",
                     help="one process on GPUs 0-1: a single multicast broadcast of BYTES from GPU 0, checked on "
                          "both GPUs (for a profiler capture of its NVLink counters)")
@@ -717,9 +717,38 @@ def main():
         dist.destroy_process_group()
         return
 
-    if args.op == "rs":
-        run_rs(args, pkg, rank, world, dev, host_group, emit)
-        return
+    # The run named on the command line, then any --also runs in the same
+    # process group (one line each; the driver's runs use the first only).
+    runs = [args]
+    for spec in [x for x in args.also.split(",") if x]:
+        r = argparse.Namespace(**vars(args))
+        r.also = ""
+        parts = spec.split(":")
+        r.op = "rs" if parts[0] == "rs" else "ag"
+        r.workload = parts[1] if r.op == "rs" and len(parts) > 1 else ("mlp70b_down" if r.op == "rs" else parts[0])
+        r.dtype = next((x for x in parts[1:] if x in ("bf16", "e4m3")), "bf16")
+        r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push")), "sm")
+        runs.append(r)
+    ok = True
+    for r in runs:
+        if r.trace and "{}" in r.trace:
+            r.trace = r.trace.format(f"{r.op}_{r.workload}_{r.dtype}_{r.producer}")
+        if r.op == "rs":
+            ok = run_rs(r, pkg, rank, world, dev, host_group, emit) and ok
+        else:
+            ok = run_ag(r, pkg, rank, world, local_rank, dev, host_group, emit) and ok
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier(group=host_group)
+        dist.destroy_process_group()
+    if not ok:
+        sys.exit(1)
+
+
+def run_ag(args, pkg, rank, world, local_rank, dev, host_group, emit):
+    """The fused all-gather GEMM on one workload; returns the parity verdict."""
+    import torch
+    import torch.distributed as dist
 
     w = WORKLOADS[args.workload]
     M, K, Ntot = w["M"], w["K"], w["N"]
@@ -949,11 +978,8 @@ def main():
     op.close()
     if rank == 0:
         emit(out)
-    if world > 1:
-        barrier()
-        dist.destroy_process_group()
-    if not out["parity"]["ok"]:
-        sys.exit(1)
+    barrier()
+    return out["parity"]["ok"]
 
 
 if __name__ == "__main__":

@@ -212,7 +212,12 @@ int agg_mp_close(agg_mp_ctx* ctx);
 /* ---- the fused all-gather GEMM ----------------------------------------------------- */
 /* Enqueue one launch on `stream`.  Shapes: M % world == 0, (M/world) % 128 == 0
    when world > 1, K % 8 == 0, N % 8 == 0 (16-byte row pitch).  Returns AGG_EINVAL
-   without launching on bad arguments. */
+   without launching on bad arguments.
+   After a launch whose status word is nonzero (a wait gave up), the slab's
+   arrival and done counters no longer match the epochs: once every rank's
+   launches have ended, zero each slab's flag area (AGG_FLAG_BYTES at flag_off)
+   and restart A_copy_epoch at 1 on every rank before launching again.  The
+   same holds for agg_launch_rs. */
 int agg_launch(const agg_args* args, void* stream);
 /* Single-GPU GEMM through the same kernel: C[M,N] = A[M,K] . B[N,K]^T (bf16). */
 int agg_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, uint32_t* status,

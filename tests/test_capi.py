@@ -135,3 +135,18 @@ def test_nvlink_counter_reader_degrades_without_nvml(pkg):
         assert "unavailable" in c.describe() and c.why
     assert nv.delta(None, (1, 2)) is None
     assert nv.delta((1, 2), (4, 7)) == (3, 5)
+
+
+def test_fused_ops_refuse_launches_after_a_failed_one(pkg):
+    """A launch that gave up leaves the slab's counters short of their epoch
+    targets; the operators then refuse to launch until a collective reset."""
+    for cls in (pkg.agg.AllGatherGemm, pkg.agg.GemmReduceScatter):
+        op = object.__new__(cls)
+        op._init_epochs()
+        op._before_launch()
+        op._before_launch()
+        assert op.epoch == 2
+        op._failed = "flag wait timed out at 3"
+        with pytest.raises(pkg.AggError, match="reset"):
+            op._before_launch()
+        assert op.epoch == 2

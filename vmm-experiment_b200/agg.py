@@ -396,7 +396,47 @@ def make_job_id(group=None) -> str:
     return obj[0]
 
 
-class AllGatherGemm:
+class _SlabEpochs:
+    """Launch bookkeeping shared by the fused operators.  Every launch on a slab
+    raises its counters by a fixed amount, and the kernels compute their wait
+    targets from the launch epoch.  A launch that gave up (nonzero status)
+    leaves the counters short, so later launches would wait for counts that
+    never come, or start early: after a failure the operator refuses to launch
+    until `reset()` (collective: every rank calls it) has zeroed the slab's
+    counters and restarted the epochs."""
+
+    def _init_epochs(self):
+        self.epoch = 0
+        self._failed = None
+
+    def _before_launch(self):
+        if self._failed:
+            raise AggError(f"a previous launch failed ({self._failed}); call reset() on every rank first")
+        self.epoch += 1
+
+    def _status_word(self):
+        word = int(self.status.item())
+        if word:
+            self._failed = describe_status(word)
+            raise AggError(f"device status: {self._failed}")
+
+    def reset(self):
+        """Collective: wait for this GPU, meet the other ranks, zero this GPU's
+        slab counters (flag area), meet again, and start the epochs over."""
+        torch = _torch()
+        torch.cuda.synchronize(self.device)
+        if self.slab is not None:
+            import torch.distributed as dist
+
+            dist.barrier(group=self._host_group)
+            device_view(self.slab.uc + self.slab.flag_off, (AGG_FLAG_BYTES,), torch.uint8, self.device).zero_()
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self._host_group)
+        self.status.zero_()
+        self._init_epochs()
+
+
+class AllGatherGemm(_SlabEpochs):
     """C_r = AllGather(A_r) . B_r^T across the ranks of torch.distributed, fused in one kernel.
 
     world == 1 (or no process group) runs the same kernel as a plain GEMM.
@@ -431,8 +471,9 @@ class AllGatherGemm:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.timeout_ns = int(timeout_s * 1e9)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.epoch = 0
+        self._init_epochs()
         self.slab = None
+        self._host_group = None
         self.double_buffer = double_buffer
         if self.world > 1:
             if m_local % AGG_TILE_M:
@@ -476,7 +517,7 @@ class AllGatherGemm:
         _check_operand(B_r, "B_r")
         if out is None:
             out = torch.empty((self.M, N), dtype=torch.bfloat16, device=self.device)
-        self.epoch += 1
+        self._before_launch()
         a = agg_args()
         a.B = B_r.data_ptr()
         a.C = out.data_ptr()
@@ -510,9 +551,7 @@ class AllGatherGemm:
         return out
 
     def check_status(self):
-        word = int(self.status.item())
-        if word:
-            raise AggError(f"device status: {describe_status(word)}")
+        self._status_word()
 
     def close(self):
         if self.slab is not None:
@@ -520,7 +559,7 @@ class AllGatherGemm:
             self.slab = None
 
 
-class GemmReduceScatter:
+class GemmReduceScatter(_SlabEpochs):
     """Y_r = rows [r*M/P, (r+1)*M/P) of sum_s X_s . W_s^T, fused in one kernel per rank.
 
     The row-parallel twin of AllGatherGemm (a tensor-parallel down projection):
@@ -546,13 +585,15 @@ class GemmReduceScatter:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.timeout_ns = int(timeout_s * 1e9)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.epoch = 0
+        self._init_epochs()
         self.slab = None
+        self._host_group = None
         self.double_buffer = double_buffer
         if m % self.world or (self.world > 1 and (m // self.world) % 256):
             raise AggError(f"M ({m}) must split into row blocks of a multiple of 256 over {self.world} ranks")
         if self.world > 1:
             hg = host_group if host_group is not None else dist.new_group(backend="gloo")
+            self._host_group = hg
             job = make_job_id(hg)
             regions = 2 if double_buffer else 1
             self.slab = MulticastSlab(self.rank, self.world, self.device.index, regions * m * n * 2, job,
@@ -576,7 +617,7 @@ class GemmReduceScatter:
             out = torch.empty((self.m_local, self.N), dtype=torch.bfloat16, device=self.device)
         if self.world == 1:
             return gemm(X_r, W_r, out=out, status=self.status, stream=stream)
-        self.epoch += 1
+        self._before_launch()
         s = self.slab
         a = agg_rs_args()
         a.X, a.W, a.Y = X_r.data_ptr(), W_r.data_ptr(), out.data_ptr()
@@ -596,9 +637,7 @@ class GemmReduceScatter:
         return out
 
     def check_status(self):
-        word = int(self.status.item())
-        if word:
-            raise AggError(f"device status: {describe_status(word)}")
+        self._status_word()
 
     def close(self):
         if self.slab is not None:

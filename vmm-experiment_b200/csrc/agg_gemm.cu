@@ -1333,15 +1333,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
 // there is one accumulator; the epilogue releases each half (tempty[0], [1])
 // as soon as it has read it, and the next tile's first MMAs into a half wait
 // only for that half.
+//
+// ST stages of 48 KiB; the epilogue stages C through EB 4 KiB buffers per warp
+// for TMA stores, or with EB = 0 writes each lane's row straight to global
+// memory (16-byte stores), so that draining the accumulator never waits for a
+// store to finish reading shared memory.
+template <int ST, int EB>
 struct WideCfg {
     static constexpr int TILE_M = 256;
     static constexpr int TILE_N = 512;
     static constexpr int A_BYTES = 128 * BK_BYTES;     // 16 KiB
     static constexpr int B_HALF = 128 * BK_BYTES;      // this CTA's 128 rows of one N half
     static constexpr int STAGE = A_BYTES + 2 * B_HALF;  // 48 KiB
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = ST;
+    static constexpr int EPI_BUFS = EB;
     static constexpr int EPI_OFF = STAGES * STAGE;
-    static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES;
+    static constexpr int BAR_OFF = EPI_OFF + EPI_WARPS * EB * EPI_BUF_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 1 + 2 + 1 + 2 * TQ_DEPTH;
     static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
     static constexpr int TQ_OFF = SLOT_OFF + 16;  // int tile ids [TQ_DEPTH]
@@ -1351,9 +1358,10 @@ struct WideCfg {
     static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0, "swizzle alignment");
 };
 
+template <int ST, int EB>
 __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             TileQueue& q, uint32_t crank, const Deadline& dl) {
-    using G = WideCfg;
+    using G = WideCfg<ST, EB>;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
     if (p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
@@ -1425,11 +1433,11 @@ __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uin
 }
 
 // The whole warp runs the loop, one elected lane issues (see pair_mma_loop).
-template <bool F8>
+template <int ST, int EB, bool F8>
 __device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
                                               uint64_t* empty, uint64_t* tfull, uint64_t* tempty, TileQueue& q,
                                               const Deadline& dl) {
-    using G = WideCfg;
+    using G = WideCfg<ST, EB>;
     constexpr uint32_t IDESC = F8 ? make_idesc(0, 0, G::TILE_M, 256) : make_idesc(1, 1, G::TILE_M, 256);
     const uint32_t lane = lane_id();
     const bool tr = p.trace != nullptr;
@@ -1505,13 +1513,14 @@ __device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, u
     }
 }
 
+template <int ST, int EB>
 __device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* full,
                                          uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
                                          TileQueue& q, const Deadline& dl) {
     if (p.dtype == AGG_DTYPE_E4M3)
-        wide_mma_loop<true>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+        wide_mma_loop<ST, EB, true>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
     else
-        wide_mma_loop<false>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
+        wide_mma_loop<ST, EB, false>(p, smem, tmem_base, full, empty, tfull, tempty, q, dl);
     umma_commit_pair_mc_warp(drain, 0x1);
     if (lane_id() == 0) {
         if (!mbar_wait_for(drain, 0, 500000000ull)) record_failure(p.status, AGG_ROLE_DRAIN, 2u);
@@ -1520,13 +1529,14 @@ __device__ __forceinline__ void wide_mma(const KParams& p, uint8_t* smem, uint32
     __syncwarp();
 }
 
+template <int ST, int EB>
 __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
                                               uint64_t* tempty, TileQueue& q, int warp, uint32_t crank,
                                               const Deadline& dl) {
-    using G = WideCfg;
+    using G = WideCfg<ST, EB>;
     const int eg = warp & 3;
     const uint32_t lane = lane_id();
-    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
+    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * EB * EPI_BUF_BYTES;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
     uint32_t acc_phase = 0;
     int buf = 0;
@@ -1591,8 +1601,21 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
                 for (int i = 0; i < 16; ++i)
                     packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
             }
-            if (col0 < p.N) {
-                if (lane == 0) bulk_wait_group_read<1>();
+            if constexpr (EB == 0) {
+                // One row per lane, 16-byte segments straight to global memory.
+                const int row = row0 + static_cast<int>(lane);
+                if (row < p.M && col0 < p.N) {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.c_ptr) +
+                                                          static_cast<size_t>(row) * p.N + col0);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        if (col0 + 8 * c < p.N)
+                            __stcs(dst + c, make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                                       packed[4 * c + 3]));
+                }
+            } else if (col0 < p.N) {
+                // The buffer is free once the TMA store issued EB chunks ago has read it.
+                if (lane == 0) bulk_wait_group_read<EB - 1>();
                 __syncwarp();
                 uint8_t* b = stg + buf * EPI_BUF_BYTES;
                 const uint32_t row_base = smem_u32(b) + lane * 128u;
@@ -1609,7 +1632,7 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
                     tma_store_2d(&p.tm_c, b, col0, row0);
                     bulk_commit_group();
                 }
-                buf ^= 1;
+                if (++buf == EB) buf = 0;
             }
         }
         acc_phase ^= 1u;
@@ -1621,8 +1644,9 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
     __syncwarp();
 }
 
+template <int ST, int EB>
 __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __grid_constant__ KParams p) {
-    using G = WideCfg;
+    using G = WideCfg<ST, EB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -1670,12 +1694,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     if (warp == 0) {
-        if (lane == 0) wide_loader(p, smem, full, empty, q, crank, dl);
+        if (lane == 0) wide_loader<ST, EB>(p, smem, full, empty, q, crank, dl);
     } else if (warp == 1) {
-        if (crank == 0) wide_mma(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
+        if (crank == 0) wide_mma<ST, EB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
     } else if (warp < 2 + EPI_WARPS) {
-        wide_epilogue(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
+        wide_epilogue<ST, EB>(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
     } else if (p.world > 1) {
         role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
@@ -1778,9 +1802,11 @@ PairKernel pair_kernel_entry(float cost) {
                       false, cost, 0};
 }
 
+template <int ST, int EB>
 PairKernel wide_kernel_entry(float cost) {
-    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_wide_kernel), WideCfg::SMEM, WideCfg::TILE_N, 128,
-                      WideCfg::STAGES, 1, true, cost, 0};
+    using G = WideCfg<ST, EB>;
+    return PairKernel{reinterpret_cast<const void*>(&ag_gemm_wide_kernel<ST, EB>), G::SMEM, G::TILE_N, 128,
+                      G::STAGES, 1, true, cost, 0};
 }
 
 constexpr int kNumPairKernels = 5;
@@ -1830,7 +1856,15 @@ int device_info(int dev, const DevInfo** out) {
         d.pair[1] = pair_kernel_entry<256, 6, 1>(1.02f);
         d.pair[2] = pair_kernel_entry<128, 4, 2>(1.12f);
         d.pair[3] = pair_kernel_entry<128, 8, 1>(1.15f);
-        d.pair[4] = wide_kernel_entry(0.93f);
+        // AGG_WIDE picks the wide kernel's stage / epilogue form: 1 (default) =
+        // 3 stages and four TMA-store buffers per warp, 0 = 4 stages and two
+        // buffers, 2 = 4 stages and direct global stores.  Sustained on the
+        // 70B MLP shape: 11.67 / 11.79 / 12.05 ms.
+        switch (env_int("AGG_WIDE", 1)) {
+            case 0: d.pair[4] = wide_kernel_entry<4, 2>(0.93f); break;
+            case 2: d.pair[4] = wide_kernel_entry<4, 0>(0.93f); break;
+            default: d.pair[4] = wide_kernel_entry<3, 4>(0.93f); break;
+        }
         d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 3, 2, true>),
                           PairCfg<256, 3, 2>::SMEM, 256, 128, 3, 2, false, 1.0f, 0};
         auto setup = [&]() -> int {
