@@ -69,6 +69,9 @@ WORKLOADS = {
     # a 4096-row x 8192-column slice of mlp70b (256 MB of operands): the case
     # the ncu captures run on
     "mlp70b_slice": dict(name="llama3-70b-mlp-slice", M=4096, K=8192, N=8192),
+    # a 9472-row x 2048-column block of mlp70b: exactly two waves of 256 x 512
+    # tiles on 148 SMs (A 155 MB + B 34 MB + C 39 MB, more than L2)
+    "mlp70b_block": dict(name="llama3-70b-mlp-block", M=9472, K=8192, N=2048),
     # the row-parallel twin (--op rs): Llama-3-70B MLP down projection, K split over ranks
     "mlp70b_down": dict(name="llama3-70b-mlp-down", M=16384, K=28672, N=8192),
 }
@@ -190,7 +193,7 @@ def wire_summary(wire, steps, ms, expected_bytes, world, group):
 
 def ncu_traffic(workload):
     """DRAM bytes per launch of the fused kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"ag_gemm_kernel_{workload}.md")
+    path = os.path.join(ROOT, "profiles", f"ag_gemm_wide_kernel_{workload}.md")
     try:
         txt = open(path).read()
     except OSError:
@@ -828,7 +831,7 @@ def run_ag(args, pkg, rank, world, local_rank, dev, host_group, emit):
     achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
     nvl_bytes = (world - 1) / world * M * K * elem if world > 1 else 0.0
     # the committed DRAM capture is of the bf16 kernel at world 1
-    traffic = ncu_traffic(args.workload) if (not f8 and world == 1) else None
+    traffic = ncu_traffic(args.workload) if (not f8 and world == 1 and not os.environ.get("AGG_KERNEL")) else None
 
     def roofline_for(peak_tc, source):
         t_tc = flops_rank / (peak_tc * 1e12)
