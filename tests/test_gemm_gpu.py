@@ -27,7 +27,7 @@ VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
             "wide": {"AGG_KERNEL": "wide"},
             "pair256n": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_RASTER_N": "1", "AGG_GROUP_M": "3"},
             "pair256rr": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "2", "AGG_SCHED": "static"}}
-ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB", "AGG_RASTER_N", "AGG_GROUP_M", "AGG_SCHED")
+ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB", "AGG_RASTER_N", "AGG_GROUP_M", "AGG_SCHED", "AGG_WIDE_SPLIT")
 
 
 @pytest.fixture(params=sorted(VARIANTS))
@@ -188,3 +188,27 @@ def test_timeout_status_reported(pkg, gpu):
     # the context is still usable
     x = torch.ones(4, device="cuda")
     assert float((x * 2).sum().item()) == 8.0
+
+
+def test_wide_kernel_last_wave_as_half_tiles(pkg, gpu, monkeypatch):
+    """80 tiles of 256 x 512 on 74 CTA pairs: the last 6 run as 12 half tiles.
+    Each half computes exactly what the whole tile computes for its columns
+    (same k order), so the output equals the unsplit launch bit for bit, and
+    matches the fp32 product within the reference's check_close."""
+    import torch
+
+    for k in ENV_KNOBS:
+        monkeypatch.delenv(k, raising=False)
+    monkeypatch.setenv("AGG_KERNEL", "wide")
+    g = torch.Generator(device="cuda").manual_seed(21)
+    M, N, K = 2560, 4000, 320  # ragged last column tile (416 of 512 columns)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    split = run_gemm(pkg, A, B)
+    monkeypatch.setenv("AGG_WIDE_SPLIT", "0")
+    whole = run_gemm(pkg, A, B)
+    assert torch.equal(split, whole)
+    ref = A.float() @ B.float().t()
+    d = (split.float() - ref).abs()
+    assert int((d > 0.1 + 0.02 * ref.abs()).sum().item()) == 0
+    assert d.max().item() <= MAX_REL * ref.abs().max().item()

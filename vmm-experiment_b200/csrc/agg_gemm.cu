@@ -128,6 +128,9 @@ struct alignas(64) KParams {
     // slot of g_sched (dynamic = 1), or round-robin by cluster (dynamic = 0).
     int sched_slot;
     int dynamic;
+    // wide kernel: work items [0, split_from) are 256 x 512 tiles, the rest
+    // halves of the remaining tiles (num_tiles counts items)
+    int split_from;
 };
 
 // Tile counters of the CTA-pair kernels' dynamic schedule.  Each launch takes
@@ -1358,6 +1361,20 @@ struct WideCfg {
     static_assert(EPI_OFF % 1024 == 0 && STAGE % 1024 == 0, "swizzle alignment");
 };
 
+// The wide kernel's work item i: a whole 256 x 512 tile (halves = 3), or, for
+// the tiles of a short last wave, one 256 x 256 half of it (halves = 1 or 2),
+// so that the last wave takes half a tile's time on twice as many pairs.
+__device__ __forceinline__ void wide_item(const KParams& p, int i, int& t, uint32_t& halves) {
+    if (i < p.split_from) {
+        t = i;
+        halves = 3u;
+        return;
+    }
+    const int j = i - p.split_from;
+    t = p.split_from + (j >> 1);
+    halves = 1u << (j & 1);
+}
+
 template <int ST, int EB>
 __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             TileQueue& q, uint32_t crank, const Deadline& dl) {
@@ -1373,13 +1390,15 @@ __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uin
     bool ok = true;
     FlagWaitLog log;
     while (ok) {
-        const int t = crank == 0 ? tq_fill(p, q, rr, dl) : tq_read(q, dl);
-        if (t == -2) {
+        const int item = crank == 0 ? tq_fill(p, q, rr, dl) : tq_read(q, dl);
+        if (item == -2) {
             record_failure(p.status, AGG_ROLE_TMA, 0xFFFFFFu);
             break;
         }
-        if (t < 0) break;
-        int mt, nt;
+        if (item < 0) break;
+        int t, mt, nt;
+        uint32_t halves;
+        wide_item(p, item, t, halves);
         tile_coords(p, t, mt, nt);
         ++log.tiles;
         const int row = mt * G::TILE_M + static_cast<int>(crank) * 128;
@@ -1410,12 +1429,13 @@ __device__ __forceinline__ void wide_loader(const KParams& p, uint8_t* smem, uin
             }
             uint8_t* sa = smem + stage * G::STAGE;
             uint8_t* sb = sa + G::A_BYTES;
-            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE);
+            if (crank == 0)
+                mbar_arrive_expect_tx(&full[stage], 2u * (G::A_BYTES + (halves == 3u ? 2u : 1u) * G::B_HALF));
             const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
             const int kx = kb * kb_elems;
             tma_load_2d_pair(tma, sa, bar, kx, a_row);
-            tma_load_2d_pair(&p.tm_b, sb, bar, kx, b_row0);
-            tma_load_2d_pair(&p.tm_b, sb + G::B_HALF, bar, kx, b_row0 + 256);
+            if (halves & 1u) tma_load_2d_pair(&p.tm_b, sb, bar, kx, b_row0);
+            if (halves & 2u) tma_load_2d_pair(&p.tm_b, sb + G::B_HALF, bar, kx, b_row0 + 256);
             used |= 1u << stage;
             last_par = (last_par & ~(1u << stage)) | (phase << stage);
             if (++stage == G::STAGES) {
@@ -1444,17 +1464,20 @@ __device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, u
     const uint64_t desc0 = sw128_kmajor_desc(smem_u32(smem));
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t acc_phase = 0;
+    uint32_t uses[2] = {0u, 0u};  // items so far that accumulated into each half
     unsigned long long full_wait = 0, full_waits = 0, acc_wait = 0;
     for (;;) {
-        int t = 0;
-        if (lane == 0) t = tq_read(q, dl);
-        t = __shfl_sync(0xffffffffu, t, 0);
-        if (t == -2) {
+        int item = 0;
+        if (lane == 0) item = tq_read(q, dl);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item == -2) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_MMA, 0xFFFFFFu);
             break;
         }
-        if (t < 0) break;
+        if (item < 0) break;
+        int t;
+        uint32_t halves;
+        wide_item(p, item, t, halves);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb && ok; ++kb) {
             if (!__all_sync(0xffffffffu, mbar_try_wait(smem_u32(&full[stage]), phase))) {
@@ -1475,10 +1498,11 @@ __device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, u
                 const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
+                    if (!((halves >> h) & 1u)) continue;
                     if (kb == 0 && k == 0) {
-                        // the epilogue must have read this half of the previous tile
+                        // the epilogue must have read this half of the last item that used it
                         const unsigned long long ta = tr ? globaltimer_ns() : 0ull;
-                        ok = mbar_wait_warp(&tempty[h], acc_phase ^ 1u, dl);
+                        ok = mbar_wait_warp(&tempty[h], (uses[h] & 1u) ^ 1u, dl);
                         if (tr) acc_wait += globaltimer_ns() - ta;
                         if (!ok) break;
                         tc_fence_after();
@@ -1504,7 +1528,7 @@ __device__ __forceinline__ void wide_mma_loop(const KParams& p, uint8_t* smem, u
             break;
         }
         umma_commit_pair_mc_warp(tfull, 0x3);
-        acc_phase ^= 1u;
+        for (int h = 0; h < 2; ++h) uses[h] += (halves >> h) & 1u;
     }
     if (tr && lane == 0) {
         trace_set(p, AGG_TR_MMA_WAIT_NS, full_wait);
@@ -1541,15 +1565,17 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
     uint32_t acc_phase = 0;
     int buf = 0;
     for (;;) {
-        int t = 0;
-        if (lane == 0) t = tq_read(q, dl);
-        t = __shfl_sync(0xffffffffu, t, 0);
-        if (t == -2) {
+        int item = 0;
+        if (lane == 0) item = tq_read(q, dl);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item == -2) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_EPI, 0xFFFFFFu);
             break;
         }
-        if (t < 0) break;
-        int mt, nt;
+        if (item < 0) break;
+        int t, mt, nt;
+        uint32_t halves;
+        wide_item(p, item, t, halves);
         tile_coords(p, t, mt, nt);
         int got = 1;
         if (lane == 0) got = mbar_wait_sleepy(tfull, acc_phase, dl) ? 1 : 0;
@@ -1564,6 +1590,7 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
         const float row_scale = f8 ? epilogue_row_scale(p, row0, lane, dl) : 1.0f;
 #pragma unroll 1
         for (int j = 0; j < G::TILE_N / EPI_COLS; ++j) {
+            if (!((halves >> (j >> 2)) & 1u)) continue;  // a half item has only one half
             uint32_t r0[32], r1[32];
             tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS), r0);
             tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS + 32), r1);
@@ -1759,6 +1786,18 @@ int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, size_t elem, const void* b
                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return check_drv(r, what);
     return AGG_OK;
+}
+
+// First tile of the wide kernel to run as two half tiles: when the last wave
+// would hold r whole tiles, and 2r half tiles still fit in one wave of
+// `clusters` pairs, the last wave takes half a tile's time instead of a whole
+// one.  AGG_WIDE_SPLIT=0 keeps whole tiles.
+int env_int(const char* name, int dflt);
+int wide_split(long tiles, int clusters) {
+    if (clusters < 1 || tiles <= clusters || env_int("AGG_WIDE_SPLIT", 1) == 0) return static_cast<int>(tiles);
+    const long r = tiles % clusters;
+    if (r == 0 || 2 * r > clusters) return static_cast<int>(tiles);
+    return static_cast<int>(tiles - r);
 }
 
 int current_sms(int* dev_out) {
@@ -1986,8 +2025,10 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
             if (!k.wide && (k.sub != sub_env || (bn_env && k.bn != bn_env))) continue;
             if (k.wide && (bn_env || sub_env != 2)) continue;
             const long tiles = static_cast<long>((a->M + 255) / 256) * ((a->N + k.bn - 1) / k.bn);
-            const long waves = (tiles + k.clusters - 1) / k.clusters;
-            const double est = static_cast<double>(waves) * 256.0 * k.bn * k.cost;
+            double waves = static_cast<double>((tiles + k.clusters - 1) / k.clusters);
+            // the wide kernel runs a short last wave as half tiles (wide_split)
+            if (k.wide && wide_split(tiles, k.clusters) < tiles) waves -= 0.5;
+            const double est = waves * 256.0 * k.bn * k.cost;
             if (!pk || est < best) {
                 pk = &k;
                 best = est;
@@ -2030,6 +2071,12 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.num_m_tiles = (a->M + tile_m - 1) / tile_m;
     p.num_n_tiles = (a->N + tile_n - 1) / tile_n;
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+    p.split_from = p.num_tiles;
+    if (pk && pk->wide) {
+        // work items: whole tiles, then the last wave's tiles as halves
+        p.split_from = wide_split(p.num_tiles, pk->clusters);
+        p.num_tiles = p.split_from + 2 * (p.num_tiles - p.split_from);
+    }
     const size_t kblock_bytes = static_cast<size_t>(BK_BYTES) * (pk ? pk->sub : 1);
     p.num_kb = static_cast<int>((static_cast<size_t>(a->K) * elem + kblock_bytes - 1) / kblock_bytes);
     // m-tiles of 256 rows per group.  One GPU: 12 (on the 16384 x 57344 x 8192
