@@ -25,9 +25,12 @@ VARIANTS = {"1sm": {"AGG_KERNEL": "1sm"},
             "pair128": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "2"},
             "pair128k1": {"AGG_KERNEL": "pair", "AGG_BN": "128", "AGG_SUB": "1"},
             "wide": {"AGG_KERNEL": "wide"},
+            "wide_tma2": {"AGG_KERNEL": "wide", "AGG_WIDE": "0"},
+            "wide_direct": {"AGG_KERNEL": "wide", "AGG_WIDE": "2"},
+            "wide_coalesced": {"AGG_KERNEL": "wide", "AGG_WIDE": "3"},
             "pair256n": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_RASTER_N": "1", "AGG_GROUP_M": "3"},
             "pair256rr": {"AGG_KERNEL": "pair", "AGG_BN": "256", "AGG_SUB": "2", "AGG_SCHED": "static"}}
-ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB", "AGG_RASTER_N", "AGG_GROUP_M", "AGG_SCHED", "AGG_WIDE_SPLIT")
+ENV_KNOBS = ("AGG_KERNEL", "AGG_BN", "AGG_SUB", "AGG_RASTER_N", "AGG_GROUP_M", "AGG_SCHED", "AGG_WIDE_SPLIT", "AGG_WIDE")
 
 
 @pytest.fixture(params=sorted(VARIANTS))

@@ -1337,10 +1337,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
 // as soon as it has read it, and the next tile's first MMAs into a half wait
 // only for that half.
 //
-// ST stages of 48 KiB; the epilogue stages C through EB 4 KiB buffers per warp
-// for TMA stores, or with EB = 0 writes each lane's row straight to global
-// memory (16-byte stores), so that draining the accumulator never waits for a
-// store to finish reading shared memory.
+// ST stages of 48 KiB.  The epilogue writes C in one of three ways:
+//   EB >= 2  stage each 32 x 64 chunk in one of EB 4 KiB buffers per warp and
+//            TMA-store it (a buffer is reused once its store has read it);
+//   EB == 1  stage the chunk in the warp's one buffer, read it back transposed
+//            (8 lanes per 128-byte row) and write whole rows with coalesced
+//            16-byte st.global: no async-proxy fence, no wait for a store to
+//            finish reading shared memory, so the accumulator drains fastest;
+//   EB == 0  each lane writes its own row straight from registers.
 template <int ST, int EB>
 struct WideCfg {
     static constexpr int TILE_M = 256;
@@ -1588,13 +1592,11 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(eg * 32) << 16);
         const int row0 = mt * G::TILE_M + static_cast<int>(crank) * 128 + eg * 32;
         const float row_scale = f8 ? epilogue_row_scale(p, row0, lane, dl) : 1.0f;
-#pragma unroll 1
-        for (int j = 0; j < G::TILE_N / EPI_COLS; ++j) {
-            if (!((halves >> (j >> 2)) & 1u)) continue;  // a half item has only one half
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS), r0);
-            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(j * EPI_COLS + 32), r1);
-            tmem_wait_ld();
+        // Chunk j: columns [64j, 64j + 64) of this warp's 32 accumulator rows.
+        // Its TMEM load is issued one chunk ahead, so the load's latency
+        // (about 400 cycles before the registers can be used) overlaps the
+        // previous chunk's conversion and stores.
+        auto chunk_out = [&](const uint32_t (&r0)[32], const uint32_t (&r1)[32], int j) {
             if ((j & 3) == 3) {
                 // this N half is read: the next tile may accumulate into it
                 tc_fence_before();
@@ -1628,7 +1630,37 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
                 for (int i = 0; i < 16; ++i)
                     packed[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
             }
-            if constexpr (EB == 0) {
+            if constexpr (EB == 1) {
+                // Rows go into the buffer one per lane (128-byte swizzle, no bank
+                // conflicts), come back 8 lanes per row, and leave as 4 whole rows
+                // per store instruction.
+                const uint32_t buf_base = smem_u32(stg);
+                const uint32_t row_base = buf_base + lane * 128u;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t addr = row_base + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[4 * c]),
+                                 "r"(packed[4 * c + 1]), "r"(packed[4 * c + 2]), "r"(packed[4 * c + 3])
+                                 : "memory");
+                }
+                __syncwarp();
+                const uint32_t seg = lane & 7u;
+                const int col = col0 + static_cast<int>(seg) * 8;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t r = static_cast<uint32_t>(i) * 4u + (lane >> 3);
+                    uint4 v;
+                    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                                 : "r"(buf_base + r * 128u + ((seg ^ (r & 7u)) << 4))
+                                 : "memory");
+                    const int row = row0 + static_cast<int>(r);
+                    if (row < p.M && col < p.N)
+                        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.c_ptr) +
+                                                  static_cast<size_t>(row) * p.N + col) = v;
+                }
+                __syncwarp();  // every lane has read the buffer before the next chunk fills it
+            } else if constexpr (EB == 0) {
                 // One row per lane, 16-byte segments straight to global memory.
                 const int row = row0 + static_cast<int>(lane);
                 if (row < p.M && col0 < p.N) {
@@ -1660,6 +1692,34 @@ __device__ __forceinline__ void wide_epilogue(const KParams& p, uint8_t* smem, u
                     bulk_commit_group();
                 }
                 if (++buf == EB) buf = 0;
+            }
+        };
+        const int jbeg = (halves & 1u) ? 0 : 4;
+        const int jend = (halves & 2u) ? 8 : 4;
+        uint32_t a0[32], a1[32], b0[32], b1[32];
+        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(jbeg * EPI_COLS), a0);
+        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(jbeg * EPI_COLS + 32), a1);
+        tmem_wait_ld();
+        regs_ready(a0);
+        regs_ready(a1);
+#pragma unroll 1
+        for (int j = jbeg; j < jend; j += 2) {  // a half has 4 chunks: they come in pairs
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((j + 1) * EPI_COLS), b0);
+            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((j + 1) * EPI_COLS + 32), b1);
+            chunk_out(a0, a1, j);
+            tmem_wait_ld();
+            regs_ready(b0);
+            regs_ready(b1);
+            const bool more = j + 2 < jend;
+            if (more) {
+                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((j + 2) * EPI_COLS), a0);
+                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((j + 2) * EPI_COLS + 32), a1);
+            }
+            chunk_out(b0, b1, j + 1);
+            if (more) {
+                tmem_wait_ld();
+                regs_ready(a0);
+                regs_ready(a1);
             }
         }
         acc_phase ^= 1u;
@@ -1848,7 +1908,10 @@ PairKernel wide_kernel_entry(float cost) {
                       G::STAGES, 1, true, cost, 0};
 }
 
-constexpr int kNumPairKernels = 5;
+// pair[0..3]: 256 x 256 / 256 x 128 forms; pair[4 + w]: the wide kernel's form w
+// (AGG_WIDE, read at each launch; kDefaultWide when unset).
+constexpr int kNumPairKernels = 9;
+constexpr int kDefaultWide = 1;
 
 // Per-device launch facts, filled once: SM count and how many CTA pairs of each
 // pair kernel can be resident at once (clusters must fit inside a GPC).
@@ -1895,15 +1958,15 @@ int device_info(int dev, const DevInfo** out) {
         d.pair[1] = pair_kernel_entry<256, 6, 1>(1.02f);
         d.pair[2] = pair_kernel_entry<128, 4, 2>(1.12f);
         d.pair[3] = pair_kernel_entry<128, 8, 1>(1.15f);
-        // AGG_WIDE picks the wide kernel's stage / epilogue form: 1 (default) =
-        // 3 stages and four TMA-store buffers per warp, 0 = 4 stages and two
-        // buffers, 2 = 4 stages and direct global stores.  Sustained on the
-        // 70B MLP shape: 11.67 / 11.79 / 12.05 ms.
-        switch (env_int("AGG_WIDE", 1)) {
-            case 0: d.pair[4] = wide_kernel_entry<4, 2>(0.93f); break;
-            case 2: d.pair[4] = wide_kernel_entry<4, 0>(0.93f); break;
-            default: d.pair[4] = wide_kernel_entry<3, 4>(0.93f); break;
-        }
+        // The wide kernel's stage / epilogue forms, by AGG_WIDE: 0 = 4 stages and
+        // two TMA-store buffers per warp, 1 = 3 stages and four, 2 = 4 stages
+        // and direct global stores, 3 = 4 stages and coalesced stores through
+        // one buffer, 4 = the same with 3 stages.
+        d.pair[4] = wide_kernel_entry<4, 2>(0.93f);
+        d.pair[5] = wide_kernel_entry<3, 4>(0.93f);
+        d.pair[6] = wide_kernel_entry<4, 0>(0.93f);
+        d.pair[7] = wide_kernel_entry<4, 1>(0.93f);
+        d.pair[8] = wide_kernel_entry<3, 1>(0.93f);
         d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 3, 2, true>),
                           PairCfg<256, 3, 2>::SMEM, 256, 128, 3, 2, false, 1.0f, 0};
         auto setup = [&]() -> int {
@@ -2017,9 +2080,12 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     if (!force_1sm && !(world > 1 && m_local % 256)) {
         const int bn_env = env_int("AGG_BN", 0);
         const int sub_env = env_int("AGG_SUB", 2);
+        const int wide_env = env_int("AGG_WIDE", kDefaultWide);
         double best = 0.0;
-        for (const PairKernel& k : di->pair) {
+        for (int ki = 0; ki < kNumPairKernels; ++ki) {
+            const PairKernel& k = di->pair[ki];
             if (k.clusters < 1) continue;
+            if (k.wide && ki - 4 != wide_env) continue;
             if (force_wide && !k.wide) continue;
             if (force_pair && k.wide) continue;
             if (!k.wide && (k.sub != sub_env || (bn_env && k.bn != bn_env))) continue;
