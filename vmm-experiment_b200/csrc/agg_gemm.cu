@@ -1276,17 +1276,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
+    // Reduce-scatter: every warp that has no GEMM work left sums owned tiles
+    // (role_reducer takes them by ticket, in completion order): the warps
+    // that produce nothing in this mode from the start, the loader, MMA and
+    // epilogue warps as soon as their part of the GEMM is done.
     if (warp == 0) {
         if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, q, crank, dl);
+        __syncwarp();
+        if constexpr (RS) role_reducer(p, dl);
     } else if (warp == 1) {
         if (crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
+        if constexpr (RS) role_reducer(p, dl);
     } else if (warp < 2 + EPI_WARPS) {
         pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
-        // Reduce-scatter: once its own tiles are out, the warp turns to summing
-        // the owned tiles (reducing next to the epilogue slowed it down).
         if constexpr (RS) role_reducer(p, dl);
-    } else if (!RS && p.world > 1) {
+    } else if constexpr (RS) {
+        role_reducer(p, dl);
+    } else if (p.world > 1) {
         role_producer(p, warp - 2 - EPI_WARPS, dl);
     }
 
