@@ -1277,13 +1277,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
     // Reduce-scatter: every warp that has no GEMM work left sums owned tiles
-    // (role_reducer takes them by ticket, in completion order): the warps
-    // that produce nothing in this mode from the start, the loader, MMA and
-    // epilogue warps as soon as their part of the GEMM is done.
+    // (role_reducer takes them by ticket, in completion order): the loader,
+    // MMA and epilogue warps as soon as their part of the GEMM is done, and
+    // the two warps that produce nothing in this mode together with the
+    // loader (named barrier 1).  Reducing from the start of the launch instead
+    // slowed the GEMM by more than it saved.
     if (warp == 0) {
         if (lane == 0) pair_loader<BN2, ST, SUB, RS>(p, smem, full, empty, q, crank, dl);
         __syncwarp();
-        if constexpr (RS) role_reducer(p, dl);
+        if constexpr (RS) {
+            named_barrier_sync(1, 3 * 32);
+            role_reducer(p, dl);
+        }
     } else if (warp == 1) {
         if (crank == 0) pair_mma<BN2, ST, SUB>(p, smem, tmem_base, full, empty, tfull, tempty, drain, q, dl);
         __syncwarp();
@@ -1292,6 +1297,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         pair_epilogue<BN2, ST, SUB, RS>(p, smem, tmem_base, tfull, tempty, q, warp, crank, dl);
         if constexpr (RS) role_reducer(p, dl);
     } else if constexpr (RS) {
+        static_assert(NUM_WARPS - 2 - EPI_WARPS == 2, "warps 0, 6, 7 meet at barrier 1");
+        named_barrier_sync(1, 3 * 32);
         role_reducer(p, dl);
     } else if (p.world > 1) {
         role_producer(p, warp - 2 - EPI_WARPS, dl);
