@@ -846,7 +846,7 @@ __device__ __forceinline__ int tq_fill(const KParams& p, TileQueue& q, int& rr, 
     return t;
 }
 
-template <int BN2, int ST, int SUB>
+template <int BN2, int ST, int SUB, int EB = 2>
 struct PairCfg {
     static constexpr int TILE_M = 256;
     static constexpr int B_ROWS = BN2 / 2;
@@ -857,10 +857,12 @@ struct PairCfg {
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int STAGES = ST;
     static constexpr int EPI_OFF = STAGES * STAGE;
-    // The epilogue stages C through swizzled smem for TMA stores when there is
-    // room; with one stage more it writes 16-byte row segments straight to HBM.
-    static constexpr bool STAGED_EPI = EPI_OFF + EPI_WARPS * 2 * EPI_BUF_BYTES + 256 + 1024 <= 232448;
-    static constexpr int BAR_OFF = EPI_OFF + (STAGED_EPI ? EPI_WARPS * 2 * EPI_BUF_BYTES : 0);
+    // The epilogue stages C through EB swizzled 4 KiB buffers per warp for TMA
+    // stores when there is room; with one stage more it writes 16-byte row
+    // segments straight to HBM.
+    static constexpr int EPI_BUFS = EB;
+    static constexpr bool STAGED_EPI = EPI_OFF + EPI_WARPS * EB * EPI_BUF_BYTES + 256 + 1024 <= 232448;
+    static constexpr int BAR_OFF = EPI_OFF + (STAGED_EPI ? EPI_WARPS * EB * EPI_BUF_BYTES : 0);
     static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1 + 2 * TQ_DEPTH;
     static constexpr int SLOT_OFF = BAR_OFF + NUM_BARS * 8;
     static constexpr int TQ_OFF = SLOT_OFF + 16;  // int tile ids [TQ_DEPTH]
@@ -871,10 +873,17 @@ struct PairCfg {
     static_assert(STAGES <= 32, "stage masks are 32-bit");
 };
 
+// The pair kernel's shared-memory layout.  The reduce-scatter twin stores its
+// partial tiles into other GPUs' memory, where a TMA store frees its staging
+// buffer only after a round trip over NVLink: it keeps four buffers per warp
+// (and 1-k-block stages to make room) so that three stores can be in flight.
+template <int BN2, int ST, int SUB, bool RS>
+using PairG = PairCfg<BN2, ST, SUB, RS ? 4 : 2>;
+
 template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_loader(const KParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                             TileQueue& q, uint32_t crank, const Deadline& dl) {
-    using G = PairCfg<BN2, ST, SUB>;
+    using G = PairG<BN2, ST, SUB, RS>;
     tma_prefetch_desc(&p.tm_a_src);
     tma_prefetch_desc(&p.tm_b);
     if (!RS && p.world > 1) tma_prefetch_desc(&p.tm_a_gath);
@@ -1067,10 +1076,10 @@ template <int BN2, int ST, int SUB, bool RS = false>
 __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, uint32_t tmem_base, uint64_t* tfull,
                                               uint64_t* tempty, TileQueue& q, int warp, uint32_t crank,
                                               const Deadline& dl) {
-    using G = PairCfg<BN2, ST, SUB>;
+    using G = PairG<BN2, ST, SUB, RS>;
     const int eg = warp & 3;
     const uint32_t lane = lane_id();
-    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * 2 * EPI_BUF_BYTES;
+    uint8_t* stg = smem + G::EPI_OFF + (warp - 2) * G::EPI_BUFS * EPI_BUF_BYTES;
     const bool f8 = p.dtype == AGG_DTYPE_E4M3;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -1158,7 +1167,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
             }
             if constexpr (G::STAGED_EPI) {
-                if (lane == 0) bulk_wait_group_read<1>();
+                if (lane == 0) bulk_wait_group_read<G::EPI_BUFS - 1>();
                 __syncwarp();
                 uint8_t* b = stg + buf * EPI_BUF_BYTES;
                 const uint32_t row_base = smem_u32(b) + lane * 128u;
@@ -1182,7 +1191,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
                     }
                     bulk_commit_group();
                 }
-                buf ^= 1;
+                if (++buf == G::EPI_BUFS) buf = 0;
             } else {
                 // One row per thread, 16-byte segments straight to global memory.
                 const int row = row0 + static_cast<int>(lane);
@@ -1228,7 +1237,7 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
 
 template <int BN2, int ST, int SUB, bool RS = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __grid_constant__ KParams p) {
-    using G = PairCfg<BN2, ST, SUB>;
+    using G = PairG<BN2, ST, SUB, RS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -1932,7 +1941,7 @@ constexpr int kDefaultWide = 1;
 struct DevInfo {
     int sms = 0;
     PairKernel pair[kNumPairKernels];
-    PairKernel rs;  // the reduce-scatter instantiation (256 x 256, 3 x 2 k-blocks)
+    PairKernel rs;  // the reduce-scatter instantiation (256 x 256, 5 stages of 1 k-block, 4 buffers)
     int rc = AGG_OK;
     std::string err;
 };
@@ -1981,8 +1990,8 @@ int device_info(int dev, const DevInfo** out) {
         d.pair[6] = wide_kernel_entry<4, 0>(0.93f);
         d.pair[7] = wide_kernel_entry<4, 1>(0.93f);
         d.pair[8] = wide_kernel_entry<3, 1>(0.93f);
-        d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 3, 2, true>),
-                          PairCfg<256, 3, 2>::SMEM, 256, 128, 3, 2, false, 1.0f, 0};
+        d.rs = PairKernel{reinterpret_cast<const void*>(&ag_gemm_pair_kernel<256, 5, 1, true>),
+                          PairG<256, 5, 1, true>::SMEM, 256, 128, 5, 1, false, 1.0f, 0};
         auto setup = [&]() -> int {
             AGG_RT(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
             AGG_RT(cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC));
