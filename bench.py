@@ -637,7 +637,7 @@ def main():
     ap.add_argument("--sweep-max", type=int, default=1 << 30)
     ap.add_argument("--sweep-ce", action="store_true",
                     help="add the copy-engine all-gathers (multicast push, push ring, pull ring) to the sweep")
-    ap.add_argument("--producer", default="sm", choices=["sm", "ce_mc", "ce_push"],
+    ap.add_argument("--producer", default="sm", choices=["sm", "ce_mc", "ce_push", "sm_peer"],
                     help="who moves the shards in the fused kernel: its producer warps (multimem.st) or the "
                          "copy engines")
     ap.add_argument("--trace", default=None, metavar="PATH",
@@ -730,7 +730,7 @@ def main():
         r.op = "rs" if parts[0] == "rs" else "ag"
         r.workload = parts[1] if r.op == "rs" and len(parts) > 1 else ("mlp70b_down" if r.op == "rs" else parts[0])
         r.dtype = next((x for x in parts[1:] if x in ("bf16", "e4m3")), "bf16")
-        r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push")), "sm")
+        r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push", "sm_peer")), "sm")
         runs.append(r)
     ok = True
     for r in runs:

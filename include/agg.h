@@ -98,6 +98,13 @@ extern "C" {
    one slab issued on the same stream. */
 #define AGG_ARGS_CE_MC_PUSH 2u         /* one copy per chunk into the multicast VA       */
 #define AGG_ARGS_CE_PEER_PUSH 4u       /* one copy per chunk and peer (order r-1, r-2..) */
+/* The kernel's producer warps store each piece of the shard into every rank's slab
+   (this GPU's included) through the unicast peer mappings A_peer[] with 16-byte
+   st.global, instead of one multimem.st into the multicast VA: the NVSwitch then
+   carries (P-1) unicast copies, which all-to-all can move faster than one multicast.
+   Needs bf16, A_peer[s] = every rank's slab base as mapped here, and A_local_buf
+   inside this rank's slab (the gathered region sits at the same offset in every slab). */
+#define AGG_ARGS_SM_PEER_PUSH 8u
 
 /* Per-rank view of the multicast slab (RankState of the reference, C layout). */
 typedef struct agg_rank_info {

@@ -115,10 +115,11 @@ def test_multicast_sweep_p2_byte_identical(mode):
             assert s["mismatched_words"] == 0, (r["rank"], s)
 
 
-@pytest.mark.parametrize("producer", ["ce_mc", "ce_push"])
+@pytest.mark.parametrize("producer", ["ce_mc", "ce_push", "sm_peer"])
 def test_copy_engine_producers_p2(producer):
-    """The fused kernel fed by copy engines instead of its producer warps:
-    chunk copies on an internal stream, arrival flags by cuStreamWriteValue32."""
+    """The fused kernel fed by copy engines instead of its producer warps
+    (chunk copies on an internal stream, arrival flags by cuStreamWriteValue32),
+    or by its producer warps storing into every peer's slab (sm_peer)."""
     res = run_ranks("ag_gemm_parity", 2, m_local=512, k=1024, n_r=512, launches=4, scheme="reference",
                     producer=producer)
     for r in res:

@@ -37,8 +37,10 @@ AGG_FLAG_USER_OFF = 72 << 10
 AGG_ARGS_DOUBLE_BUFFER = 1
 AGG_ARGS_CE_MC_PUSH = 2
 AGG_ARGS_CE_PEER_PUSH = 4
+AGG_ARGS_SM_PEER_PUSH = 8
 AGG_CE_MC_PUSH, AGG_CE_PEER_PUSH, AGG_CE_PEER_PULL = 0, 1, 2
-PRODUCERS = {"sm": 0, "ce_mc": AGG_ARGS_CE_MC_PUSH, "ce_push": AGG_ARGS_CE_PEER_PUSH}
+PRODUCERS = {"sm": 0, "ce_mc": AGG_ARGS_CE_MC_PUSH, "ce_push": AGG_ARGS_CE_PEER_PUSH,
+             "sm_peer": AGG_ARGS_SM_PEER_PUSH}
 ROLE_NAMES = {1: "tma", 2: "mma", 3: "epilogue", 4: "flag", 5: "producer", 6: "barrier", 7: "drain",
               8: "reducer"}
 AGG_TRACE_SLOTS = 16
@@ -449,16 +451,20 @@ class AllGatherGemm(_SlabEpochs):
     def __init__(self, m_local: int, k: int, *, dtype: str = "bf16", group=None, device=None,
                  timeout_s: float = 10.0, host_group=None, double_buffer: bool = True, producer: str = "sm"):
         """`producer` chooses who moves this rank's shard: "sm" (the kernel's own
-        warps, multimem.st; default), "ce_mc" (copy engines, one copy per chunk
-        into the multicast VA) or "ce_push" (copy engines, one copy per chunk and
-        peer); the copy-engine modes need bf16 and double buffering."""
+        warps, multimem.st; default), "sm_peer" (the same warps, one 16-byte
+        store per rank through the unicast peer mappings; bf16), "ce_mc" (copy
+        engines, one copy per chunk into the multicast VA) or "ce_push" (copy
+        engines, one copy per chunk and peer); the copy-engine modes need bf16
+        and double buffering."""
         torch = _torch()
         import torch.distributed as dist
 
         if producer not in PRODUCERS:
             raise AggError(f"producer must be one of {sorted(PRODUCERS)}")
-        if producer != "sm" and (dtype != "bf16" or not double_buffer):
+        if producer.startswith("ce") and (dtype != "bf16" or not double_buffer):
             raise AggError("copy-engine producers need bf16 and double buffering")
+        if producer == "sm_peer" and dtype != "bf16":
+            raise AggError("the SM peer push moves bf16 shards only")
         self.producer = producer
         self.dtype = dtype
         self.elem = 1 if dtype == "e4m3" else 2

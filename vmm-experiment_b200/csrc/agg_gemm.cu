@@ -124,6 +124,8 @@ struct alignas(64) KParams {
     __nv_bfloat16* y;        // this rank's rows of the sum [M/world, N]
     uint32_t rs_target;      // a tile's partials are all stored when its counter reaches this
     int ext_producer;        // 1: copy engines move the shard (AGG_ARGS_CE_*), no producer warps
+    int peer_push;           // 1: producers store into every rank's slab (AGG_ARGS_SM_PEER_PUSH)
+    uint64_t peer_dst[AGG_MAX_RANKS];  // peer_push: this rank's slot in every rank's slab, this launch's region
     // CTA-pair kernels: tiles are handed out in raster order from this launch's
     // slot of g_sched (dynamic = 1), or round-robin by cluster (dynamic = 0).
     int sched_slot;
@@ -584,10 +586,22 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
                     const unsigned long long j = i + 32ull * u;
                     if (j < n) v[u] = ld_nc_v4(s + j);
                 }
+                if (p.peer_push) {
+                    // one unicast copy per rank (this GPU's own slot included), the
+                    // ranks interleaved so every link carries traffic at once
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const unsigned long long j = i + 32ull * u;
-                    if (j < n) mm_st_v4(d + j, v[u]);
+                    for (int u = 0; u < 8; ++u) {
+                        const unsigned long long j = i + 32ull * u;
+                        if (j < n)
+                            for (int r = 0; r < p.world; ++r)
+                                reinterpret_cast<uint4*>(p.peer_dst[r] + beg)[j] = v[u];
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const unsigned long long j = i + 32ull * u;
+                        if (j < n) mm_st_v4(d + j, v[u]);
+                    }
                 }
             }
         }
@@ -2066,6 +2080,17 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
         if (a->A_copy_epoch < 1) return fail(AGG_EINVAL, "agg_launch: epoch must start at 1");
     }
     const uint32_t ce_mode = a->flags & (AGG_ARGS_CE_MC_PUSH | AGG_ARGS_CE_PEER_PUSH);
+    const bool peer_push = world > 1 && (a->flags & AGG_ARGS_SM_PEER_PUSH) != 0;
+    if (peer_push) {
+        if (ce_mode) return fail(AGG_EINVAL, "agg_launch: choose the copy engines or the SM peer push");
+        if (f8) return fail(AGG_EINVAL, "agg_launch: the SM peer push moves bf16 shards only");
+        for (int s = 0; s < world; ++s)
+            if (!a->A_peer[s] || a->A_peer[s] % 16)
+                return fail(AGG_EINVAL, "agg_launch: the SM peer push needs A_peer[%d] (16-byte aligned)", s);
+        const uint64_t lb = reinterpret_cast<uint64_t>(a->A_local_buf);
+        if (lb < a->A_peer[a->dev_idx] || (lb - a->A_peer[a->dev_idx]) % 16)
+            return fail(AGG_EINVAL, "agg_launch: A_local_buf must lie in this rank's slab (A_peer[rank])");
+    }
     if (ce_mode && world > 1) {
         if (ce_mode == (AGG_ARGS_CE_MC_PUSH | AGG_ARGS_CE_PEER_PUSH))
             return fail(AGG_EINVAL, "agg_launch: choose one copy-engine mode");
@@ -2183,6 +2208,14 @@ int launch_ag_gemm(const agg_args* a, cudaStream_t stream) {
     p.epoch = a->A_copy_epoch;
 
     if (world > 1) {
+        if (peer_push) {
+            // the gathered region sits at the same offset in every rank's slab
+            const uint64_t goff = reinterpret_cast<uint64_t>(a->A_local_buf) - a->A_peer[a->dev_idx];
+            p.peer_push = 1;
+            for (int s = 0; s < world; ++s)
+                p.peer_dst[s] = a->A_peer[s] + goff + region_off +
+                                static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem;
+        }
         p.a_mc = reinterpret_cast<uint4*>(a->A_mc + region_off +
                                           static_cast<uint64_t>(a->dev_idx) * m_local * a->K * elem);
         p.shard_bytes = static_cast<unsigned long long>(m_local) * a->K * elem;
