@@ -637,9 +637,10 @@ def main():
     ap.add_argument("--sweep-max", type=int, default=1 << 30)
     ap.add_argument("--sweep-ce", action="store_true",
                     help="add the copy-engine all-gathers (multicast push, push ring, pull ring) to the sweep")
-    ap.add_argument("--producer", default="sm", choices=["sm", "ce_mc", "ce_push", "sm_peer"],
-                    help="who moves the shards in the fused kernel: its producer warps (multimem.st) or the "
-                         "copy engines")
+    ap.add_argument("--producer", default="auto", choices=["auto", "sm", "ce_mc", "ce_push", "sm_peer"],
+                    help="who moves the shards in the fused kernel: its producer warps by one multicast "
+                         "store (sm) or by a store per peer (sm_peer), or the copy engines; auto: sm_peer for "
+                         "bf16 on 2-4 GPUs, sm otherwise")
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
     ap.add_argument("--also", default="", metavar="RUNS",
@@ -730,7 +731,7 @@ def main():
         r.op = "rs" if parts[0] == "rs" else "ag"
         r.workload = parts[1] if r.op == "rs" and len(parts) > 1 else ("mlp70b_down" if r.op == "rs" else parts[0])
         r.dtype = next((x for x in parts[1:] if x in ("bf16", "e4m3")), "bf16")
-        r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push", "sm_peer")), "sm")
+        r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push", "sm_peer")), "auto")
         runs.append(r)
     ok = True
     for r in runs:
@@ -852,7 +853,8 @@ def run_ag(args, pkg, rank, world, local_rank, dev, host_group, emit):
            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": args.dtype,
            "data": "synthetic (A~N(0,1), B~N(0,0.02), seeded per rank)" + (", per-row amax e4m3" if f8 else ""),
-           "config": config_of(args.workload, world, args.dtype), "tflops_per_gpu": value / world,
+           "config": dict(config_of(args.workload, world, args.dtype), producer=op.producer),
+           "tflops_per_gpu": value / world,
            "gpu_launches": args.steps, "roofline": roofline, "clocks": clk}
     if wire is not None:
         out["nvlink_counters"] = wire_summary(wire, args.steps, ms, nvl_bytes, world, host_group)

@@ -449,18 +449,25 @@ class AllGatherGemm(_SlabEpochs):
     """
 
     def __init__(self, m_local: int, k: int, *, dtype: str = "bf16", group=None, device=None,
-                 timeout_s: float = 10.0, host_group=None, double_buffer: bool = True, producer: str = "sm"):
+                 timeout_s: float = 10.0, host_group=None, double_buffer: bool = True, producer: str = "auto"):
         """`producer` chooses who moves this rank's shard: "sm" (the kernel's own
         warps, multimem.st; default), "sm_peer" (the same warps, one 16-byte
         store per rank through the unicast peer mappings; bf16), "ce_mc" (copy
         engines, one copy per chunk into the multicast VA) or "ce_push" (copy
         engines, one copy per chunk and peer); the copy-engine modes need bf16
-        and double buffering."""
+        and double buffering.  "auto" (default) picks "sm_peer" for bf16 on 2-4
+        ranks and "sm" otherwise: measured on the fused kernel, the unicast
+        stores win up to P = 4 (the multicast path delivers 345-540 GB/s of
+        ingress per GPU there) and lose at P = 8, where their 7x egress from
+        the SMs competes with the GEMM."""
         torch = _torch()
         import torch.distributed as dist
 
+        if producer == "auto":
+            w = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+            producer = "sm_peer" if dtype == "bf16" and 2 <= w <= 4 else "sm"
         if producer not in PRODUCERS:
-            raise AggError(f"producer must be one of {sorted(PRODUCERS)}")
+            raise AggError(f"producer must be one of {sorted(PRODUCERS) + ['auto']}")
         if producer.startswith("ce") and (dtype != "bf16" or not double_buffer):
             raise AggError("copy-engine producers need bf16 and double buffering")
         if producer == "sm_peer" and dtype != "bf16":
