@@ -469,7 +469,11 @@ def run_rs(args, pkg, rank, world, dev, host_group, emit):
     X_r = torch.randn(M, k_r, device=dev, generator=g).bfloat16()
     W_r = (torch.randn(N, k_r, device=dev, generator=g) * 0.02).bfloat16()
     Y_r = torch.empty(m_local, N, device=dev, dtype=torch.bfloat16)
-    op = pkg.GemmReduceScatter(M, N, k_r, host_group=host_group)
+    if args.ce_streams:  # read by the library at each launch
+        os.environ["AGG_RS_CE_STREAMS"] = str(args.ce_streams)
+    else:
+        os.environ.pop("AGG_RS_CE_STREAMS", None)
+    op = pkg.GemmReduceScatter(M, N, k_r, host_group=host_group, exchange=args.exchange)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -525,7 +529,9 @@ def run_rs(args, pkg, rank, world, dev, host_group, emit):
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (X~N(0,1), W~N(0,0.02), seeded per rank)",
            "config": {"workload": w["name"], "M": M, "K_total": Ktot, "K_per_rank": k_r, "N": N,
                       "M_out_per_rank": m_local, "P": world, "l2": "inputs larger than L2, no flush",
-                      "parallelism": f"rs-tp{world}"},
+                      "parallelism": f"rs-tp{world}", "exchange": op.exchange if world > 1 else None,
+                      "copy_streams": int(os.environ.get("AGG_RS_CE_STREAMS", "1"))
+                      if world > 1 and op.exchange == "ce" else None},
            "tflops_per_gpu": value / world, "gpu_launches": args.steps, "roofline": roofline, "clocks": clk}
     if wire is not None:
         out["nvlink_counters"] = wire_summary(wire, args.steps, ms, nvl_bytes, world, host_group)
@@ -643,9 +649,15 @@ def main():
                          "bf16 on 2-4 GPUs, sm otherwise")
     ap.add_argument("--trace", default=None, metavar="PATH",
                     help="after timing, trace one launch per rank and write the per-event summary to PATH")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "sm", "ce"],
+                    help="--op rs: who moves the partials, the epilogue's TMA stores into the owners' inboxes "
+                         "(sm) or the copy engines from a local stage (ce); auto: ce")
+    ap.add_argument("--ce-streams", type=int, default=0,
+                    help="--op rs --exchange ce: internal copy streams per block (1-4; 0: the library default)")
     ap.add_argument("--also", default="", metavar="RUNS",
                     help="comma-separated further runs in the same process group after the first, each "
-                         "WORKLOAD[:e4m3][:ce_mc|ce_push] or rs[:WORKLOAD]; one result line each")
+                         "WORKLOAD[:e4m3][:sm|sm_peer|ce_mc|ce_push] or rs[:WORKLOAD][:sm|ce][:sN] (N copy "
+                         "streams); one result line each")
     ap.add_argument("--nvlink-probe", type=int, default=0, metavar="BYTES",
                     help="one process on GPUs 0-1: a single multicast broadcast of BYTES from GPU 0, checked on "
                          "both GPUs (for a profiler capture of its NVLink counters)")
@@ -729,14 +741,20 @@ def main():
         r.also = ""
         parts = spec.split(":")
         r.op = "rs" if parts[0] == "rs" else "ag"
-        r.workload = parts[1] if r.op == "rs" and len(parts) > 1 else ("mlp70b_down" if r.op == "rs" else parts[0])
+        if r.op == "rs":
+            r.workload = next((x for x in parts[1:] if x in WORKLOADS), "mlp70b_down")
+            r.exchange = next((x for x in parts[1:] if x in ("sm", "ce")), "auto")
+            r.ce_streams = next((int(x[1:]) for x in parts[1:] if x[:1] == "s" and x[1:].isdigit()), 0)
+        else:
+            r.workload = parts[0]
         r.dtype = next((x for x in parts[1:] if x in ("bf16", "e4m3")), "bf16")
         r.producer = next((x for x in parts[1:] if x in ("sm", "ce_mc", "ce_push", "sm_peer")), "auto")
         runs.append(r)
     ok = True
     for r in runs:
         if r.trace and "{}" in r.trace:
-            r.trace = r.trace.format(f"{r.op}_{r.workload}_{r.dtype}_{r.producer}")
+            mode = f"{r.exchange}{r.ce_streams or ''}" if r.op == "rs" else r.producer
+            r.trace = r.trace.format(f"{r.op}_{r.workload}_{r.dtype}_{mode}")
         if r.op == "rs":
             ok = run_rs(r, pkg, rank, world, dev, host_group, emit) and ok
         else:

@@ -171,8 +171,10 @@ typedef struct agg_args {
 #define AGG_TR_PROD_DONE 2      /* this CTA's producers pushed all their parts        */
 #define AGG_TR_FIRST_WAIT 3     /* loader starts its first wait for a remote chunk    */
 #define AGG_TR_FIRST_READY 4    /* ... and sees it                                    */
-#define AGG_TR_LAST_READY 5     /* loader sees its last remote chunk                  */
+#define AGG_TR_LAST_READY 5     /* loader sees its last remote chunk (reduce-scatter  */
+                                /* copy-engine exchange: reducers see every block)    */
 #define AGG_TR_FLAG_WAIT_NS 6   /* total time the loader waited on remote chunks      */
+                                /* (... the reducers waited for the blocks)           */
 #define AGG_TR_LOADER_DONE 7    /* loader issued its last k-block                     */
 #define AGG_TR_MMA_DONE 8       /* tensor-core issuer committed its last tile         */
 #define AGG_TR_EPI_DONE 9       /* epilogue stored its last tile                      */
@@ -274,7 +276,24 @@ int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, i
  * AGG_ARGS_DOUBLE_BUFFER, region 1 right after region 0) at the same offset in
  * every rank's slab.  Counters and the done counter live in the slab's flag area
  * (AGG_FLAG_CHUNK_OFF, AGG_FLAG_DONE_OFF).
+ *
+ * With AGG_ARGS_RS_COPY_ENGINE the SMs store nothing to a peer: the kernel
+ * visits the owners' row blocks in the order rank+1, rank+2, ..., rank itself
+ * last and TMA-stores the partials of the other owners into `stage` (this
+ * GPU's memory, [M, N] bf16, block s at rows [s*M/P, (s+1)*M/P)).  An internal
+ * stream waits (cuStreamWaitValue32) until each owner's block is stored, copies
+ * it into slot `rank` of that owner's inbox with cudaMemcpyAsync and writes the
+ * owner's arrival word for this source (cuStreamWriteValue32 through the peer
+ * mapping); the owner's reducers wait for all P-1 arrival words, then add the
+ * slots of each of its own tiles as they complete.  A launch that fails marks
+ * itself failed in every peer's flag area before it releases the copies, so
+ * the owners fail too instead of reducing a partial sum.  The launch completes
+ * on `stream` once the copies have.  All launches on one slab use one mode.
+ * Flag area words (after AGG_FLAG_DONE_OFF): +256 B u32 [AGG_MAX_RANKS] slices
+ * stored per owner, +320 B arrival words per source, +384 B failure marks per
+ * source.
  */
+#define AGG_ARGS_RS_COPY_ENGINE 16u
 typedef struct agg_rs_args {
     const void* X;        /* this rank's activation slice [M, K] bf16, K-major       */
     const void* W;        /* this rank's weight slice [N, K] bf16, K-major           */
@@ -288,10 +307,12 @@ typedef struct agg_rs_args {
     uint32_t epoch;       /* launch ordinal on this slab: 1, 2, ... on every rank     */
     int32_t rank, world;
     int32_t M, N, K;      /* K: this rank's slice of the contraction                  */
-    uint32_t flags;       /* AGG_ARGS_DOUBLE_BUFFER                                   */
+    uint32_t flags;       /* AGG_ARGS_DOUBLE_BUFFER | AGG_ARGS_RS_COPY_ENGINE         */
     uint32_t* status;     /* device status word, may be NULL                          */
     uint64_t timeout_ns;  /* bound on every device-side wait; 0 = 10 s                */
     uint64_t* trace;      /* optional: u64 [grid][AGG_TRACE_SLOTS] event times (ns)   */
+    void* stage;          /* AGG_ARGS_RS_COPY_ENGINE: [M, N] bf16 on this GPU, 16-byte */
+                          /* aligned; the other owners' partial blocks before the copy */
 } agg_rs_args;
 
 /* Enqueue one launch on `stream`; AGG_EINVAL without launching on bad arguments. */

@@ -174,10 +174,13 @@ def ag_gemm_changing_inputs(rank, world, port, m_local, k, n_r, launches, produc
         _teardown(op)
 
 
-def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=True):
+def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=True, exchange="auto",
+                   compare_exchange=None):
     """Fused GEMM + reduce-scatter vs the oracle: launch e uses X_s, W_s drawn by
     fill_random from seeds 5000 + 100e + s and 6000 + s (U[-1, 1], bf16); rank r's
-    output must be rows [r*M/P, (r+1)*M/P) of sum_s X_s . W_s^T."""
+    output must be rows [r*M/P, (r+1)*M/P) of sum_s X_s . W_s^T.  With
+    `compare_exchange`, a second operator using that exchange runs the same
+    launches and its outputs must be bit-identical (same partials, same order)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -185,20 +188,28 @@ def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=
     import oracle
 
     pkg = _init(rank, world, port)
-    op = None
+    op = other = None
     try:
         M = world * m_per_rank
         Ws = [oracle.fill_random_bf16(6000 + s, n * k) for s in range(world)]
-        op = pkg.GemmReduceScatter(M, n, k, host_group=dist.group.WORLD, double_buffer=double_buffer)
+        op = pkg.GemmReduceScatter(M, n, k, host_group=dist.group.WORLD, double_buffer=double_buffer,
+                                   exchange=exchange)
+        if compare_exchange:
+            other = pkg.GemmReduceScatter(M, n, k, host_group=dist.group.WORLD, double_buffer=double_buffer,
+                                          exchange=compare_exchange)
         W_r = _bits_to_dev(Ws[rank][0], (n, k))
-        outs, inputs = [], []
+        outs, inputs, identical = [], [], True
         for e in range(launches):
             Xs = [oracle.fill_random_bf16(5000 + 100 * e + s, M * k) for s in range(world)]
             inputs.append(Xs)
             X_r = _bits_to_dev(Xs[rank][0], (M, k))
             outs.append(op(X_r, W_r))
+            if other is not None:
+                identical = identical and torch.equal(other(X_r, W_r), outs[-1])
         torch.cuda.synchronize()
         op.check_status()
+        if other is not None:
+            other.check_status()
         worst, bad_total, bound_total, nan_total = 0.0, 0, 0, 0
         rows = slice(rank * m_per_rank, (rank + 1) * m_per_rank)
         for e in range(launches):
@@ -218,9 +229,9 @@ def gemm_rs_parity(rank, world, port, m_per_rank, n, k, launches, double_buffer=
             bad_total += bad
             nan_total += stats["nan"]
         return {"rank": rank, "worst_rel_err": worst, "bad_check_close": bad_total, "bad": bound_total,
-                "nan": nan_total, "epoch": op.epoch}
+                "nan": nan_total, "epoch": op.epoch, "exchange": op.exchange, "identical": identical}
     finally:
-        _teardown(op)
+        _teardown(op, other)
 
 
 def torch_ops_mlp(rank, world, port, m, k, n):

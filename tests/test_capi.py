@@ -104,6 +104,14 @@ def test_reduce_scatter_layout_and_argument_checks(pkg):
     assert launch(peers=(0x10000, 0x20008)) == -1
     assert launch(M=2 * 256 * 64, N=256 * 129) == -1   # more tiles than counters
     assert b"tiles" in L.agg_last_error()
+    ce = agg.AGG_ARGS_RS_COPY_ENGINE
+    assert launch(flags=ce, status=0x8000) == -1                  # copy-engine exchange without a stage
+    assert b"stage" in L.agg_last_error()
+    assert launch(flags=ce, status=0x8000, stage=0x9008) == -1    # stage not 16-byte aligned
+    assert launch(flags=ce, stage=0x9000) == -1                   # ... or without a status word
+    assert b"status" in L.agg_last_error()
+    assert launch(flags=ce, status=0x8000, stage=0x9000, done_uc=0x10000) == -1  # flags before the inbox
+    assert b"done_uc" in L.agg_last_error()
 
 
 def test_errors_without_gpu_are_reported_not_raised(pkg):

@@ -138,15 +138,31 @@ def test_multimem_known_answers_p2():
         assert r["barrier_status"] == 0 and r["barrier_flags_ok"], r
 
 
+@pytest.mark.parametrize("exchange", ["sm", "ce"])
 @pytest.mark.parametrize("double_buffer", [True, False])
-def test_gemm_reduce_scatter_p2(double_buffer):
+def test_gemm_reduce_scatter_p2(double_buffer, exchange):
     """The row-parallel twin: bf16 partial tiles in each slab, the owner's rows
-    summed through NVSwitch.  Ragged N and K; new activations every launch.
-    Tolerance: max rel err <= 1e-2, and per element the reference's check_close
-    (atol 0.1, rtol 0.02) widened by the bf16 rounding of each rank's partial
-    (2^-8 * sum of |partial|), the same rounding a bf16 NCCL reduce-scatter does."""
-    res = run_ranks("gemm_rs_parity", 2, m_per_rank=512, n=520, k=264, launches=3, double_buffer=double_buffer)
+    summed from its inbox; the partials moved by the epilogue's TMA stores
+    ("sm") or by copy engines from a local stage ("ce").  Ragged N and K; new
+    activations every launch.  Tolerance: max rel err <= 1e-2, and per element
+    the reference's check_close (atol 0.1, rtol 0.02) widened by the bf16
+    rounding of each rank's partial (2^-8 * sum of |partial|), the same
+    rounding a bf16 NCCL reduce-scatter does."""
+    res = run_ranks("gemm_rs_parity", 2, m_per_rank=512, n=520, k=264, launches=3, double_buffer=double_buffer,
+                    exchange=exchange)
     for r in res:
+        assert r["exchange"] == exchange
+        assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
+
+
+def test_gemm_reduce_scatter_exchanges_bit_identical_p2():
+    """Both exchanges add the same bf16 partials in the same source order: their
+    outputs agree bit for bit, launch after launch, with several m-tiles per
+    owner block (1024 rows per rank) and a ragged last n-tile."""
+    res = run_ranks("gemm_rs_parity", 2, m_per_rank=1024, n=776, k=520, launches=3, exchange="ce",
+                    compare_exchange="sm")
+    for r in res:
+        assert r["identical"], r
         assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
 
 
@@ -162,8 +178,9 @@ def test_torch_ops_mlp_p2():
 def test_gemm_reduce_scatter_wider(world):
     if n_gpus() < world:
         pytest.skip(f"needs {world} GPUs")
-    res = run_ranks("gemm_rs_parity", world, m_per_rank=256, n=1024, k=512, launches=2)
+    res = run_ranks("gemm_rs_parity", world, m_per_rank=256, n=1024, k=512, launches=2, compare_exchange="sm")
     for r in res:
+        assert r["identical"], r
         assert r["nan"] == 0 and r["bad"] == 0 and r["worst_rel_err"] <= 1e-2, r
 
 

@@ -38,6 +38,7 @@ AGG_ARGS_DOUBLE_BUFFER = 1
 AGG_ARGS_CE_MC_PUSH = 2
 AGG_ARGS_CE_PEER_PUSH = 4
 AGG_ARGS_SM_PEER_PUSH = 8
+AGG_ARGS_RS_COPY_ENGINE = 16
 AGG_CE_MC_PUSH, AGG_CE_PEER_PUSH, AGG_CE_PEER_PULL = 0, 1, 2
 PRODUCERS = {"sm": 0, "ce_mc": AGG_ARGS_CE_MC_PUSH, "ce_push": AGG_ARGS_CE_PEER_PUSH,
              "sm_peer": AGG_ARGS_SM_PEER_PUSH}
@@ -150,6 +151,7 @@ class agg_rs_args(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
         ("trace", ctypes.c_void_p),
+        ("stage", ctypes.c_void_p),
     ]
 
 
@@ -582,13 +584,28 @@ class GemmReduceScatter(_SlabEpochs):
     adds the slots of each of its tiles (fp32, source order) as they complete.
     world == 1 runs the plain GEMM.  With `double_buffer` (default) the slab
     holds two [M, N] partial regions used by launch parity.
+
+    `exchange` chooses who moves the partials to their owners: "sm" (the
+    epilogue warps TMA-store them into the owners' inboxes over NVLink) or
+    "ce" (the epilogue stores them into a local stage in owner order and the
+    copy engines copy each owner's block as soon as it is complete, so the SMs
+    only do the GEMM and the reduction; needs an extra [M, N] bf16 buffer).
+    "auto" (default) picks "ce".
     """
 
+    EXCHANGES = ("sm", "ce")
+
     def __init__(self, m: int, n: int, k_local: int, *, group=None, device=None, timeout_s: float = 10.0,
-                 host_group=None, double_buffer: bool = True):
+                 host_group=None, double_buffer: bool = True, exchange: str = "auto"):
         torch = _torch()
         import torch.distributed as dist
 
+        if exchange == "auto":
+            exchange = "ce"
+        if exchange not in self.EXCHANGES:
+            raise AggError(f"unknown exchange {exchange!r} (one of {', '.join(self.EXCHANGES)} or auto)")
+        self.exchange = exchange
+        self.stage = None
         self.M, self.N, self.k = m, n, k_local
         if dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(group)
@@ -611,6 +628,8 @@ class GemmReduceScatter(_SlabEpochs):
             regions = 2 if double_buffer else 1
             self.slab = MulticastSlab(self.rank, self.world, self.device.index, regions * m * n * 2, job,
                                       _default_group_barrier(hg))
+            if exchange == "ce":
+                self.stage = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
 
     @property
     def m_local(self) -> int:
@@ -642,6 +661,9 @@ class GemmReduceScatter(_SlabEpochs):
         a.rank, a.world = self.rank, self.world
         a.M, a.N, a.K = self.M, self.N, self.k
         a.flags = AGG_ARGS_DOUBLE_BUFFER if self.double_buffer else 0
+        if self.stage is not None:
+            a.flags |= AGG_ARGS_RS_COPY_ENGINE
+            a.stage = self.stage.data_ptr()
         a.status = self.status.data_ptr()
         a.timeout_ns = self.timeout_ns
         if trace is not None:
@@ -656,3 +678,4 @@ class GemmReduceScatter(_SlabEpochs):
         if self.slab is not None:
             self.slab.close()
             self.slab = None
+        self.stage = None

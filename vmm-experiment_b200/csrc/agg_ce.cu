@@ -13,7 +13,12 @@
 //                            (the write is ordered after the copy by the stream
 //                            and carries a memory barrier), while the kernel's
 //                            loaders wait on those flags exactly as they wait on
-//                            the multimem producers'.
+//                            the multimem producers';
+//   * ce_rs_exchange       — the reduce-scatter twin's exchange in the same way,
+//                            the other direction: the internal stream waits
+//                            (cuStreamWaitValue32) for the kernel to store each
+//                            owner's partial block, copies it into the owner's
+//                            inbox and writes the owner's arrival word.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -26,13 +31,18 @@
 namespace agg {
 namespace {
 
-// One internal stream and two events per device, created on first use.
+// Internal streams and events per device, created on first use: `stream`
+// carries the copies; the reduce-scatter exchange can spread each copy over
+// `extra` streams too (more copy engines), joined back through `ev_join`.
+constexpr int kCeExtra = 3;
 struct CeDev {
     std::once_flag once;
     std::mutex mu;
     int rc = AGG_OK;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    cudaStream_t extra[kCeExtra] = {};
+    cudaEvent_t ev_join[kCeExtra] = {};
 };
 CeDev g_ce[64];
 
@@ -44,6 +54,10 @@ int ce_dev(int dev, CeDev** out) {
             AGG_RT(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
             AGG_RT(cudaEventCreateWithFlags(&c.ev_in, cudaEventDisableTiming));
             AGG_RT(cudaEventCreateWithFlags(&c.ev_out, cudaEventDisableTiming));
+            for (int i = 0; i < kCeExtra; ++i) {
+                AGG_RT(cudaStreamCreateWithFlags(&c.extra[i], cudaStreamNonBlocking));
+                AGG_RT(cudaEventCreateWithFlags(&c.ev_join[i], cudaEventDisableTiming));
+            }
             return AGG_OK;
         };
         c.rc = setup();
@@ -66,6 +80,14 @@ int write_u32(uint64_t addr, uint32_t value, cudaStream_t s) {
     return AGG_OK;
 }
 
+int wait_geq_u32(const uint32_t* addr, uint32_t value, cudaStream_t s) {
+    const DriverApi& d = driver();
+    if (!d.ok) return fail(AGG_EDRIVER, "CUDA driver unavailable: %s", d.why.c_str());
+    AGG_DRV(d.cuStreamWaitValue32(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(addr), value,
+                                  CU_STREAM_WAIT_VALUE_GEQ));
+    return AGG_OK;
+}
+
 }  // namespace
 
 // Orders the internal stream after everything enqueued on `caller` so far
@@ -79,6 +101,7 @@ int ce_begin(cudaStream_t caller, cudaStream_t* ce) {
     c->mu.lock();
     cudaError_t e = cudaEventRecord(c->ev_in, caller);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->ev_in, 0);
+    for (int i = 0; i < kCeExtra && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(c->extra[i], c->ev_in, 0);
     if (e != cudaSuccess) {
         c->mu.unlock();
         return check_rt(e, "copy-engine stream ordering");
@@ -92,7 +115,12 @@ int ce_end(cudaStream_t caller) {
     int dev = 0;
     AGG_RT(cudaGetDevice(&dev));
     CeDev& c = g_ce[dev];
-    cudaError_t e = cudaEventRecord(c.ev_out, c.stream);
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < kCeExtra && e == cudaSuccess; ++i) {
+        e = cudaEventRecord(c.ev_join[i], c.extra[i]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c.stream, c.ev_join[i], 0);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(c.ev_out, c.stream);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(caller, c.ev_out, 0);
     c.mu.unlock();
     if (e != cudaSuccess) return check_rt(e, "copy-engine completion");
@@ -131,6 +159,36 @@ int ce_push_shard(const agg_args* a, const void* src, int m_local, size_t row_by
                 rc = write_u32(a->A_peer[d] + flag_off + 4 * word, target, ce);
             }
         }
+    }
+    return rc;
+}
+
+int ce_rs_exchange(int rank, int world, const uint64_t* inbox_slot, const uint8_t* stage, size_t slot_bytes,
+                   uint32_t* cnt, uint32_t target, const uint64_t* rx_word, uint32_t epoch, int streams,
+                   cudaStream_t ce) {
+    int dev = 0;
+    AGG_RT(cudaGetDevice(&dev));
+    CeDev& c = g_ce[dev];  // held by ce_begin: `ce` is c.stream
+    const int n = std::max(1, std::min(streams, 1 + kCeExtra));
+    // piece i of a block: bytes [i * piece, min((i + 1) * piece, slot_bytes)), 16-byte aligned
+    const size_t piece = (slot_bytes / n + 15) / 16 * 16;
+    int rc = AGG_OK;
+    for (int b = 1; b < world && rc == AGG_OK; ++b) {
+        const int s = (rank + b) % world;
+        const uint8_t* src = stage + static_cast<size_t>(s) * slot_bytes;
+        for (int i = 0; i < n && rc == AGG_OK; ++i) {
+            const size_t beg = static_cast<size_t>(i) * piece;
+            if (beg >= slot_bytes) break;
+            const size_t bytes = std::min(piece, slot_bytes - beg);
+            cudaStream_t st = i == 0 ? ce : c.extra[i - 1];
+            rc = wait_geq_u32(cnt + s, target, st);
+            if (rc == AGG_OK) rc = copy(inbox_slot[s] + beg, src + beg, bytes, st);
+            if (rc == AGG_OK && i > 0) {
+                AGG_RT(cudaEventRecord(c.ev_join[i - 1], st));
+                AGG_RT(cudaStreamWaitEvent(ce, c.ev_join[i - 1], 0));
+            }
+        }
+        if (rc == AGG_OK) rc = write_u32(rx_word[s], epoch, ce);  // after every piece of the block
     }
     return rc;
 }

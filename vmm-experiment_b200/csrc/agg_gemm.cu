@@ -126,6 +126,13 @@ struct alignas(64) KParams {
     int ext_producer;        // 1: copy engines move the shard (AGG_ARGS_CE_*), no producer warps
     int peer_push;           // 1: producers store into every rank's slab (AGG_ARGS_SM_PEER_PUSH)
     uint64_t peer_dst[AGG_MAX_RANKS];  // peer_push: this rank's slot in every rank's slab, this launch's region
+    // reduce-scatter with the copy-engine exchange (AGG_ARGS_RS_COPY_ENGINE)
+    int rs_ce;                  // 1: other owners' partials go to the local stage; copy engines move them
+    uint32_t* ce_cnt;           // this GPU's slices stored per owner, u32 [AGG_MAX_RANKS]
+    const uint32_t* ce_rx;      // this GPU's arrival words, per source rank (written by the sources' copies)
+    const uint32_t* ce_fail;    // this GPU's failure marks, per source rank
+    uint64_t ce_fail_peer[AGG_MAX_RANKS];  // this rank's failure mark in every rank's flag area
+    uint32_t ce_target;         // ce_cnt[s] once owner s's block of this launch is stored
     // CTA-pair kernels: tiles are handed out in raster order from this launch's
     // slot of g_sched (dynamic = 1), or round-robin by cluster (dynamic = 0).
     int sched_slot;
@@ -193,7 +200,30 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& mt, in
 // `group_m` m positions as above, where position pos is local m-tile pos / P
 // of owner pos % P, so that every owner's tiles complete at an even rate on all
 // ranks at once and its reducers always have finished tiles to work on.
+// With the copy-engine exchange the order is owner-major instead: owner
+// rank+1's block, then rank+2's, ..., this rank's own block last, each in
+// groups of `group_m` m-tiles; a block is copied out as soon as it is stored.
+__device__ __forceinline__ void rs_block_tile(const KParams& p, int owner, int j, int& mt, int& nt) {
+    const int L = p.m_local / 256;
+    const int gm = min(p.group_m, L);
+    const int per_group = gm * p.num_n_tiles;
+    const int g = j / per_group;
+    j -= g * per_group;
+    const int first = g * gm;
+    const int gs = min(gm, L - first);
+    nt = j / gs;
+    mt = owner * L + first + (j - nt * gs);
+}
+
 __device__ __forceinline__ void rs_tile_coords(const KParams& p, int t, int& mt, int& nt) {
+    if (p.rs_ce) {
+        const int per_owner = (p.m_local / 256) * p.num_n_tiles;
+        const int b = t / per_owner;
+        int owner = p.rank + 1 + b;
+        if (owner >= p.world) owner -= p.world;
+        rs_block_tile(p, owner, t - b * per_owner, mt, nt);
+        return;
+    }
     const int per_group = p.group_m * p.num_n_tiles;
     const int g = t / per_group;
     const int j = t - g * per_group;
@@ -643,12 +673,34 @@ __device__ __forceinline__ void role_producer(const KParams& p, int pw, const De
 // local memory in source order (fp32), one 16-byte load per lane, row and
 // slot.  (Pulling the sum through NVSwitch with multimem.ld_reduce instead
 // moved only ~100 GB/s and stalled the SMs.)
+//
+// With the copy-engine exchange the other ranks' slots arrive as whole blocks:
+// a reducer first waits (once) for every source's arrival word, then for each
+// tile only for this rank's own partial (stored last, in rs_block_tile order).
+__device__ __forceinline__ bool rs_ce_sources_arrived(const KParams& p, const Deadline& dl) {
+    for (int s = 0; s < p.world; ++s) {
+        if (s == p.rank) continue;
+        for (uint32_t spin = 0;; ++spin) {
+            if (ld_relaxed_sys(p.ce_fail + s) >= p.epoch) return false;
+            if (ld_relaxed_sys(p.ce_rx + s) >= p.epoch) break;
+            __nanosleep(500);
+            if ((spin & 15u) == 15u && (globaltimer_ns() > dl.end_ns || failed(dl.status))) return false;
+        }
+    }
+    fence_acq_rel_sys();
+    // a source that failed marks it before it releases its copies
+    for (int s = 0; s < p.world; ++s)
+        if (s != p.rank && ld_relaxed_sys(p.ce_fail + s) >= p.epoch) return false;
+    return true;
+}
+
 __device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& dl) {
     const uint32_t lane = lane_id();
     const int L = p.m_local / 256;
     const int nN = p.num_n_tiles;
     const int P = p.world;
     const unsigned long long units = static_cast<unsigned long long>(L) * nN * 8ull;
+    bool sources = !p.rs_ce;  // copy-engine exchange: the other ranks' blocks are in
     for (;;) {
         unsigned long long ticket = 0;
         if (lane == 0) ticket = atomicAdd(p.ticket, 1ull);
@@ -656,23 +708,39 @@ __device__ __forceinline__ void role_reducer(const KParams& p, const Deadline& d
         if (ticket >= units) break;
         const int slice = static_cast<int>(ticket & 7ull);
         int k = static_cast<int>(ticket >> 3);
-        // k-th owned tile in completion order: walk the m-position groups.
-        int pos = -1, nt = 0;
-        for (int first = 0; first < p.num_m_tiles; first += p.group_m) {
-            const int gs = min(p.group_m, p.num_m_tiles - first);
-            const int f_own = first + ((p.rank - first) % P + P) % P;  // first owned position >= first
-            const int owned = f_own < first + gs ? (first + gs - 1 - f_own) / P + 1 : 0;
-            if (k < owned * nN) {
-                nt = k / owned;
-                pos = f_own + (k - nt * owned) * P;
-                break;
+        int mt = -1, nt = 0;
+        if (p.rs_ce) {
+            rs_block_tile(p, p.rank, k, mt, nt);
+        } else {
+            // k-th owned tile in completion order: walk the m-position groups.
+            for (int first = 0; first < p.num_m_tiles; first += p.group_m) {
+                const int gs = min(p.group_m, p.num_m_tiles - first);
+                const int f_own = first + ((p.rank - first) % P + P) % P;  // first owned position >= first
+                const int owned = f_own < first + gs ? (first + gs - 1 - f_own) / P + 1 : 0;
+                if (k < owned * nN) {
+                    nt = k / owned;
+                    mt = p.rank * L + (f_own + (k - nt * owned) * P) / P;
+                    break;
+                }
+                k -= owned * nN;
             }
-            k -= owned * nN;
         }
-        if (pos < 0) break;  // not reached: units counts exactly the owned tiles
-        const int mt = p.rank * L + pos / P;
+        if (mt < 0) break;  // not reached: units counts exactly the owned tiles
         int ok = 1;
-        if (lane == 0) ok = wait_flag_geq_quiet(p.flags_uc + mt * nN + nt, p.rs_target, dl) ? 1 : 0;
+        if (!sources) {
+            if (lane == 0) {
+                const unsigned long long t0 = p.trace ? globaltimer_ns() : 0ull;
+                ok = rs_ce_sources_arrived(p, dl) ? 1 : 0;
+                if (p.trace) {  // when this CTA's reducers had every block, and how long they waited
+                    const unsigned long long t1 = globaltimer_ns();
+                    trace_max(p, AGG_TR_LAST_READY, t1);
+                    atomicAdd(p.trace + blockIdx.x * AGG_TRACE_SLOTS + AGG_TR_FLAG_WAIT_NS, t1 - t0);
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            sources = true;
+        }
+        if (lane == 0 && ok) ok = wait_flag_geq_quiet(p.flags_uc + mt * nN + nt, p.rs_target, dl) ? 1 : 0;
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) {
             if (lane == 0) record_failure(p.status, AGG_ROLE_REDUCE, static_cast<uint32_t>(mt * nN + nt));
@@ -789,6 +857,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
+            if (p.rs_ce && failed(p.status)) {
+                // The copy stream waits for every owner's block: mark this launch
+                // failed in every peer's flag area, then release the waits, so
+                // that the owners give up instead of adding what the copies bring.
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
+                fence_acq_rel_sys();
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
+            }
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
@@ -1080,9 +1158,18 @@ __device__ __forceinline__ void pair_mma(const KParams& p, uint8_t* smem, uint32
 // Reduce-scatter: one warp's slice of tile `tile` has landed in the owner's
 // inbox (its TMA stores completed): order it before the count, then raise the
 // tile's counter on every GPU.
+//
+// With the copy-engine exchange a slice of another owner's tile has landed in
+// the local stage: count it on this GPU's counter for that owner, which the
+// copy stream waits on.  A slice of an own tile is counted on this GPU only.
 __device__ __forceinline__ void rs_publish(const KParams& p, int tile) {
     fence_proxy_async_global();
     fence_acq_rel_sys();
+    if (p.rs_ce) {
+        const int owner = tile / p.num_n_tiles / (p.m_local / 256);
+        red_add_release_sys_u32(owner == p.rank ? p.flags_uc + tile : p.ce_cnt + owner, 1u);
+        return;
+    }
     mm_red_add_release_u32(p.flags_mc + tile, 1u);
 }
 
@@ -1356,6 +1443,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
+            if (p.rs_ce && failed(p.status)) {
+                // The copy stream waits for every owner's block: mark this launch
+                // failed in every peer's flag area, then release the waits, so
+                // that the owners give up instead of adding what the copies bring.
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
+                fence_acq_rel_sys();
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
+            }
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
@@ -1853,6 +1950,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
+            if (p.rs_ce && failed(p.status)) {
+                // The copy stream waits for every owner's block: mark this launch
+                // failed in every peer's flag area, then release the waits, so
+                // that the owners give up instead of adding what the copies bring.
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
+                fence_acq_rel_sys();
+                for (int s = 0; s < p.world; ++s)
+                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
+            }
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);
             fence_acq_rel_sys();
@@ -2311,6 +2418,13 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
         if (!a->part_peer[s] || a->part_peer[s] % 16)
             return fail(AGG_EINVAL, "agg_launch_rs: inbox of rank %d missing or not 16-byte aligned", s);
     if (a->epoch < 1) return fail(AGG_EINVAL, "agg_launch_rs: epoch must start at 1");
+    const bool ce = (a->flags & AGG_ARGS_RS_COPY_ENGINE) != 0;
+    if (ce && (!a->stage || reinterpret_cast<uintptr_t>(a->stage) % 16))
+        return fail(AGG_EINVAL, "agg_launch_rs: the copy-engine exchange needs a 16-byte aligned stage [M, N]");
+    if (ce && !a->status)
+        return fail(AGG_EINVAL, "agg_launch_rs: the copy-engine exchange needs a status word");
+    if (ce && reinterpret_cast<uint64_t>(a->done_uc) <= a->part_peer[a->rank])
+        return fail(AGG_EINVAL, "agg_launch_rs: done_uc must lie in this rank's slab, after its inbox");
     const int num_m_tiles = a->M / 256;
     const int num_n_tiles = (a->N + 255) / 256;
     if (static_cast<long long>(num_m_tiles) * num_n_tiles > AGG_RS_MAX_TILES)
@@ -2335,11 +2449,16 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->W, a->K, a->N, kb_elems, di->rs.b_box,
                    "tensor map W");
     if (rc) return rc;
-    // Slot `rank` of owner s's inbox (in its slab, as mapped here): rows of s's block.
+    // Slot `rank` of owner s's inbox (in its slab, as mapped here): rows of s's
+    // block.  With the copy-engine exchange, the other owners' blocks go to the
+    // local stage instead, at their own rows.
     const size_t slot_bytes = static_cast<size_t>(m_local) * a->N * 2;
+    uint64_t inbox_slot[AGG_MAX_RANKS] = {};
     for (int s = 0; s < world; ++s) {
-        rc = encode_2d(&p.tm_out[s], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                       reinterpret_cast<const void*>(a->part_peer[s] + parity * region + a->rank * slot_bytes), a->N,
+        inbox_slot[s] = a->part_peer[s] + parity * region + a->rank * slot_bytes;
+        const uint64_t dst = (ce && s != a->rank) ? reinterpret_cast<uint64_t>(a->stage) + s * slot_bytes
+                                                   : inbox_slot[s];
+        rc = encode_2d(&p.tm_out[s], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, reinterpret_cast<const void*>(dst), a->N,
                        m_local, EPI_COLS, EPI_ROWS, "tensor map inbox");
         if (rc) return rc;
     }
@@ -2373,7 +2492,33 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     p.ticket = reinterpret_cast<unsigned long long*>(a->done_uc + 32);  // +128 B
     p.inbox = reinterpret_cast<const uint8_t*>(a->part_peer[a->rank] + parity * region);
     p.y = static_cast<__nv_bfloat16*>(a->Y);
-    return launch_pair(di->rs, p, stream, dev);
+    if (!ce) return launch_pair(di->rs, p, stream, dev);
+
+    // Copy-engine exchange.  Own tiles count 8 slices per launch of their
+    // parity on this GPU only; the per-owner counters 8 slices per tile of the
+    // owner's block per launch.
+    p.rs_ce = 1;
+    p.rs_target = 8u * ordinal;
+    p.ce_target = 8u * static_cast<uint32_t>(m_local / 256) * static_cast<uint32_t>(num_n_tiles) * e;
+    p.ce_cnt = a->done_uc + 64;   // +256 B
+    p.ce_rx = a->done_uc + 80;    // +320 B
+    p.ce_fail = a->done_uc + 96;  // +384 B
+    // the flag area sits at the same offset from the inbox in every slab
+    const uint64_t flag_rel = reinterpret_cast<uint64_t>(a->done_uc) - a->part_peer[a->rank];
+    uint64_t rx_word[AGG_MAX_RANKS] = {};
+    for (int s = 0; s < world; ++s) {
+        p.ce_fail_peer[s] = a->part_peer[s] + flag_rel + 4u * (96u + static_cast<uint32_t>(a->rank));
+        rx_word[s] = a->part_peer[s] + flag_rel + 4u * (80u + static_cast<uint32_t>(a->rank));
+    }
+    cudaStream_t cs = nullptr;
+    rc = ce_begin(stream, &cs);  // before the launch: the copy stream must not wait for the kernel to end
+    if (rc) return rc;
+    rc = launch_pair(di->rs, p, stream, dev);
+    if (rc == AGG_OK)
+        rc = ce_rs_exchange(a->rank, world, inbox_slot, static_cast<const uint8_t*>(a->stage), slot_bytes, p.ce_cnt,
+                            p.ce_target, rx_word, e, env_int("AGG_RS_CE_STREAMS", 1), cs);
+    const int rc_end = ce_end(stream);
+    return rc ? rc : rc_end;
 }
 
 }  // namespace agg

@@ -178,6 +178,14 @@ __device__ __forceinline__ bool wait_flag_geq_quiet(const uint32_t* flag, uint32
     }
 }
 
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_add_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ------------------------------------------------------------------ proxy fences
 __device__ __forceinline__ void fence_proxy_alias() {
     asm volatile("fence.proxy.alias;" ::: "memory");
