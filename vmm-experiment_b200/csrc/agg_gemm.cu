@@ -1313,8 +1313,15 @@ __device__ __forceinline__ void pair_epilogue(const KParams& p, uint8_t* smem, u
             // its TMA stores have landed, which the warp checks only after issuing
             // the next tile's stores: the wait then leaves that tile's
             // BN2/EPI_COLS store groups in flight.
+            // With the copy-engine exchange every store is local and lands within
+            // a microsecond or two, far inside the next tile's MMA time: the warp
+            // waits for it and counts the slice at once, so that a block's copy
+            // and an own tile's reduction do not wait a tile longer.
             static_assert(G::STAGED_EPI, "reduce-scatter publishes TMA-stored slices");
-            if (lane == 0) {
+            if (lane == 0 && p.rs_ce) {
+                bulk_wait_group<0>();
+                rs_publish(p, mt * p.num_n_tiles + nt);
+            } else if (lane == 0) {
                 if (rs_pending >= 0) {
                     bulk_wait_group<BN2 / EPI_COLS>();
                     rs_publish(p, rs_pending);
