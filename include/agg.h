@@ -279,19 +279,21 @@ int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, i
  *
  * With AGG_ARGS_RS_COPY_ENGINE the SMs store nothing to a peer: the kernel
  * visits the owners' row blocks in the order rank+1, rank+2, ..., rank itself
- * last and TMA-stores the partials of the other owners into `stage` (this
- * GPU's memory, [M, N] bf16, block s at rows [s*M/P, (s+1)*M/P)).  An internal
- * stream waits (cuStreamWaitValue32) until each owner's block is stored, copies
- * it into slot `rank` of that owner's inbox with cudaMemcpyAsync and writes the
- * owner's arrival word for this source (cuStreamWriteValue32 through the peer
- * mapping); the owner's reducers wait for all P-1 arrival words, then add the
+ * last, each in chunks of 2 m-tiles (512 rows; AGG_RS_CE_GROUP overrides), and
+ * TMA-stores the partials of the other owners into `stage` (this GPU's memory,
+ * [M, N] bf16, block s at rows [s*M/P, (s+1)*M/P)).  An internal stream waits
+ * (cuStreamWaitValue32) until each chunk is stored, copies it into slot `rank`
+ * of that owner's inbox with cudaMemcpyAsync and, after a block's last chunk,
+ * writes the owner's arrival word for this source (cuStreamWriteValue32
+ * through the peer mapping); the owner's reducers wait for all P-1 arrival
+ * words, then add the
  * slots of each of its own tiles as they complete.  A launch that fails marks
  * itself failed in every peer's flag area before it releases the copies, so
  * the owners fail too instead of reducing a partial sum.  The launch completes
  * on `stream` once the copies have.  All launches on one slab use one mode.
- * Flag area words (after AGG_FLAG_DONE_OFF): +256 B u32 [AGG_MAX_RANKS] slices
- * stored per owner, +320 B arrival words per source, +384 B failure marks per
- * source.
+ * Flag area words (after AGG_FLAG_DONE_OFF): +320 B arrival words per source,
+ * +384 B failure marks per source, +4 KiB u32 [AGG_MAX_RANKS][chunks] slices
+ * stored per owner and chunk (at most 128 chunks per owner).
  */
 #define AGG_ARGS_RS_COPY_ENGINE 16u
 typedef struct agg_rs_args {

@@ -164,31 +164,34 @@ int ce_push_shard(const agg_args* a, const void* src, int m_local, size_t row_by
 }
 
 int ce_rs_exchange(int rank, int world, const uint64_t* inbox_slot, const uint8_t* stage, size_t slot_bytes,
-                   uint32_t* cnt, uint32_t target, const uint64_t* rx_word, uint32_t epoch, int streams,
-                   cudaStream_t ce) {
+                   size_t m_tile_bytes, int L, int gm, int n_tiles, uint32_t* cnt, const uint64_t* rx_word,
+                   uint32_t epoch, int streams, cudaStream_t ce) {
     int dev = 0;
     AGG_RT(cudaGetDevice(&dev));
     CeDev& c = g_ce[dev];  // held by ce_begin: `ce` is c.stream
     const int n = std::max(1, std::min(streams, 1 + kCeExtra));
-    // piece i of a block: bytes [i * piece, min((i + 1) * piece, slot_bytes)), 16-byte aligned
-    const size_t piece = (slot_bytes / n + 15) / 16 * 16;
+    const int chunks = (L + gm - 1) / gm;
     int rc = AGG_OK;
     for (int b = 1; b < world && rc == AGG_OK; ++b) {
         const int s = (rank + b) % world;
         const uint8_t* src = stage + static_cast<size_t>(s) * slot_bytes;
-        for (int i = 0; i < n && rc == AGG_OK; ++i) {
-            const size_t beg = static_cast<size_t>(i) * piece;
-            if (beg >= slot_bytes) break;
-            const size_t bytes = std::min(piece, slot_bytes - beg);
+        bool used[1 + kCeExtra] = {};
+        for (int k = 0; k < chunks && rc == AGG_OK; ++k) {
+            const int rows = std::min(gm, L - k * gm);
+            const size_t beg = static_cast<size_t>(k) * gm * m_tile_bytes;
+            const uint32_t target = 8u * static_cast<uint32_t>(rows) * static_cast<uint32_t>(n_tiles) * epoch;
+            const int i = k % n;
             cudaStream_t st = i == 0 ? ce : c.extra[i - 1];
-            rc = wait_geq_u32(cnt + s, target, st);
-            if (rc == AGG_OK) rc = copy(inbox_slot[s] + beg, src + beg, bytes, st);
-            if (rc == AGG_OK && i > 0) {
-                AGG_RT(cudaEventRecord(c.ev_join[i - 1], st));
-                AGG_RT(cudaStreamWaitEvent(ce, c.ev_join[i - 1], 0));
-            }
+            used[i] = true;
+            rc = wait_geq_u32(cnt + s * chunks + k, target, st);
+            if (rc == AGG_OK) rc = copy(inbox_slot[s] + beg, src + beg, static_cast<size_t>(rows) * m_tile_bytes, st);
         }
-        if (rc == AGG_OK) rc = write_u32(rx_word[s], epoch, ce);  // after every piece of the block
+        for (int i = 1; i < n && rc == AGG_OK; ++i) {
+            if (!used[i]) continue;
+            AGG_RT(cudaEventRecord(c.ev_join[i - 1], c.extra[i - 1]));
+            AGG_RT(cudaStreamWaitEvent(ce, c.ev_join[i - 1], 0));
+        }
+        if (rc == AGG_OK) rc = write_u32(rx_word[s], epoch, ce);  // after every chunk of the block
     }
     return rc;
 }

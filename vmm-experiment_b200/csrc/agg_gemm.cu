@@ -128,11 +128,11 @@ struct alignas(64) KParams {
     uint64_t peer_dst[AGG_MAX_RANKS];  // peer_push: this rank's slot in every rank's slab, this launch's region
     // reduce-scatter with the copy-engine exchange (AGG_ARGS_RS_COPY_ENGINE)
     int rs_ce;                  // 1: other owners' partials go to the local stage; copy engines move them
-    uint32_t* ce_cnt;           // this GPU's slices stored per owner, u32 [AGG_MAX_RANKS]
+    uint32_t* ce_cnt;           // this GPU's slices stored per owner and chunk, u32 [AGG_MAX_RANKS][ce_chunks]
+    int ce_chunks;              // chunks per owner block: groups of min(group_m, m_local/256) m-tiles
     const uint32_t* ce_rx;      // this GPU's arrival words, per source rank (written by the sources' copies)
     const uint32_t* ce_fail;    // this GPU's failure marks, per source rank
     uint64_t ce_fail_peer[AGG_MAX_RANKS];  // this rank's failure mark in every rank's flag area
-    uint32_t ce_target;         // ce_cnt[s] once owner s's block of this launch is stored
     // CTA-pair kernels: tiles are handed out in raster order from this launch's
     // slot of g_sched (dynamic = 1), or round-robin by cluster (dynamic = 0).
     int sched_slot;
@@ -232,6 +232,26 @@ __device__ __forceinline__ void rs_tile_coords(const KParams& p, int t, int& mt,
     nt = j / gs;
     const int pos = first + (j - nt * gs);
     mt = (pos % p.world) * (p.m_local / 256) + pos / p.world;
+}
+
+// Copy-engine exchange, a launch that gave up: the copy stream waits for
+// every chunk of every owner's block.  Mark this launch failed in every peer's
+// flag area, then release the waits (each chunk counter to its target: 8
+// slices x its tiles x epoch), so that the owners give up instead of adding
+// what the copies bring.  Run by the last CTA, after every other CTA is done.
+__device__ __noinline__ void rs_ce_release(const KParams& p) {
+    for (int s = 0; s < p.world; ++s)
+        if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
+    fence_acq_rel_sys();
+    const int L = p.m_local / 256;
+    const int gm = min(p.group_m, L);
+    for (int s = 0; s < p.world; ++s) {
+        if (s == p.rank) continue;
+        for (int c = 0; c < p.ce_chunks; ++c) {
+            const uint32_t rows = static_cast<uint32_t>(min(gm, L - c * gm));
+            atomicExch(p.ce_cnt + s * p.ce_chunks + c, 8u * rows * static_cast<uint32_t>(p.num_n_tiles) * p.epoch);
+        }
+    }
 }
 
 // ---- optional event trace (one row of AGG_TRACE_SLOTS u64 per CTA)
@@ -857,16 +877,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_kernel(const __grid_co
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
-            if (p.rs_ce && failed(p.status)) {
-                // The copy stream waits for every owner's block: mark this launch
-                // failed in every peer's flag area, then release the waits, so
-                // that the owners give up instead of adding what the copies bring.
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
-                fence_acq_rel_sys();
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
-            }
+            if (p.rs_ce && failed(p.status)) rs_ce_release(p);
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
@@ -1166,8 +1177,11 @@ __device__ __forceinline__ void rs_publish(const KParams& p, int tile) {
     fence_proxy_async_global();
     fence_acq_rel_sys();
     if (p.rs_ce) {
-        const int owner = tile / p.num_n_tiles / (p.m_local / 256);
-        red_add_release_sys_u32(owner == p.rank ? p.flags_uc + tile : p.ce_cnt + owner, 1u);
+        const int L = p.m_local / 256;
+        const int mt = tile / p.num_n_tiles;
+        const int owner = mt / L;
+        const int chunk = (mt - owner * L) / min(p.group_m, L);  // the group of m-tiles rs_block_tile runs together
+        red_add_release_sys_u32(owner == p.rank ? p.flags_uc + tile : p.ce_cnt + owner * p.ce_chunks + chunk, 1u);
         return;
     }
     mm_red_add_release_u32(p.flags_mc + tile, 1u);
@@ -1450,16 +1464,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_pair_kernel(const __gr
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
-            if (p.rs_ce && failed(p.status)) {
-                // The copy stream waits for every owner's block: mark this launch
-                // failed in every peer's flag area, then release the waits, so
-                // that the owners give up instead of adding what the copies bring.
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
-                fence_acq_rel_sys();
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
-            }
+            if (p.rs_ce && failed(p.status)) rs_ce_release(p);
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);  // every producer of this launch is done
             fence_acq_rel_sys();
@@ -1957,16 +1962,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ag_gemm_wide_kernel(const __gr
         __threadfence();
         const uint32_t prev = atomicAdd(p.cta_counter, 1u);
         if (prev == gridDim.x - 1u) {
-            if (p.rs_ce && failed(p.status)) {
-                // The copy stream waits for every owner's block: mark this launch
-                // failed in every peer's flag area, then release the waits, so
-                // that the owners give up instead of adding what the copies bring.
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) st_relaxed_sys_u32(reinterpret_cast<uint32_t*>(p.ce_fail_peer[s]), p.epoch);
-                fence_acq_rel_sys();
-                for (int s = 0; s < p.world; ++s)
-                    if (s != p.rank) atomicExch(p.ce_cnt + s, p.ce_target);
-            }
+            if (p.rs_ce && failed(p.status)) rs_ce_release(p);
             atomicExch(p.cta_counter, 0u);
             atomicExch(p.ticket, 0ull);
             fence_acq_rel_sys();
@@ -2502,13 +2498,21 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     if (!ce) return launch_pair(di->rs, p, stream, dev);
 
     // Copy-engine exchange.  Own tiles count 8 slices per launch of their
-    // parity on this GPU only; the per-owner counters 8 slices per tile of the
-    // owner's block per launch.
+    // parity on this GPU only.  Each owner's block runs as chunks of gm m-tiles
+    // (all n-tiles of a chunk before the next), counted per (owner, chunk): 8
+    // slices per tile per launch, so a chunk's copy can start as soon as it is
+    // stored.  Two m-tiles (256 rows x N x 2 bytes each: 8 MiB per chunk at
+    // N = 8192) start the copies about a block earlier than whole blocks; at
+    // most 128 chunks per owner fit the counter area (flag area + 4 KiB).
+    const int L = m_local / 256;
+    int gm = std::max(1, std::min(L, env_int("AGG_RS_CE_GROUP", 2)));
+    gm = std::max(gm, (L + 127) / 128);
+    p.group_m = gm;
     p.rs_ce = 1;
     p.rs_target = 8u * ordinal;
-    p.ce_target = 8u * static_cast<uint32_t>(m_local / 256) * static_cast<uint32_t>(num_n_tiles) * e;
-    p.ce_cnt = a->done_uc + 64;   // +256 B
-    p.ce_rx = a->done_uc + 80;    // +320 B
+    p.ce_chunks = (L + gm - 1) / gm;
+    p.ce_cnt = a->done_uc + 1024;  // +4 KiB: u32 [AGG_MAX_RANKS][ce_chunks]
+    p.ce_rx = a->done_uc + 80;     // +320 B
     p.ce_fail = a->done_uc + 96;  // +384 B
     // the flag area sits at the same offset from the inbox in every slab
     const uint64_t flag_rel = reinterpret_cast<uint64_t>(a->done_uc) - a->part_peer[a->rank];
@@ -2522,8 +2526,9 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     if (rc) return rc;
     rc = launch_pair(di->rs, p, stream, dev);
     if (rc == AGG_OK)
-        rc = ce_rs_exchange(a->rank, world, inbox_slot, static_cast<const uint8_t*>(a->stage), slot_bytes, p.ce_cnt,
-                            p.ce_target, rx_word, e, env_int("AGG_RS_CE_STREAMS", 1), cs);
+        rc = ce_rs_exchange(a->rank, world, inbox_slot, static_cast<const uint8_t*>(a->stage), slot_bytes,
+                            static_cast<size_t>(256) * a->N * 2, L, gm, num_n_tiles, p.ce_cnt, rx_word, e,
+                            env_int("AGG_RS_CE_STREAMS", 1), cs);
     const int rc_end = ce_end(stream);
     return rc ? rc : rc_end;
 }

@@ -67,16 +67,17 @@ int ce_end(cudaStream_t caller);
 int ce_push_shard(const agg_args* a, const void* src, int m_local, size_t row_bytes, uint64_t region_off,
                   uint32_t parity, uint32_t target, bool multicast, cudaStream_t ce);
 // The reduce-scatter twin's copy-engine exchange, on the internal stream `ce`:
-// for owners rank+1, rank+2, ... (the kernel's block order), wait until
-// cnt[owner] >= target (the kernel has stored the owner's block in `stage`,
-// at the owner's rows), copy the block into inbox_slot[owner] (slot `rank` of
-// that owner's inbox, as mapped here) and write `epoch` into rx_word[owner]
-// (this source's arrival word in the owner's flag area).  Each copy is split
-// into `streams` pieces (1-4) on as many internal streams, which the write
-// waits for.
+// for owners rank+1, rank+2, ... (the kernel's block order) and each chunk c
+// of gm m-tiles (m_tile_bytes each, L per block) of the owner's block, wait
+// until cnt[owner * chunks + c] >= 8 x tiles of the chunk x epoch (the kernel
+// has stored the chunk in `stage`, at the owner's rows), copy it into
+// inbox_slot[owner] (slot `rank` of that owner's inbox, as mapped here); after
+// the block's last chunk write `epoch` into rx_word[owner] (this source's
+// arrival word in the owner's flag area).  Chunk c goes on internal stream
+// c % streams (1-4); the write waits for all of them.
 int ce_rs_exchange(int rank, int world, const uint64_t* inbox_slot, const uint8_t* stage, size_t slot_bytes,
-                   uint32_t* cnt, uint32_t target, const uint64_t* rx_word, uint32_t epoch, int streams,
-                   cudaStream_t ce);
+                   size_t m_tile_bytes, int L, int gm, int n_tiles, uint32_t* cnt, const uint64_t* rx_word,
+                   uint32_t epoch, int streams, cudaStream_t ce);
 
 }  // namespace agg
 
