@@ -279,8 +279,8 @@ int agg_gemm_bf16_noalloc(const void* A, const void* B, void* C, int M, int N, i
  *
  * With AGG_ARGS_RS_COPY_ENGINE the SMs store nothing to a peer: the kernel
  * visits the owners' row blocks in the order rank+1, rank+2, ..., rank itself
- * last, each in chunks of 2 m-tiles (512 rows) when W fits in 64 MiB, else of
- * 12 (AGG_RS_CE_GROUP overrides; fixed for all launches on a slab), and
+ * last, each in chunks of 12 m-tiles (a whole block when M/P <= 3072;
+ * AGG_RS_CE_GROUP overrides, fixed for all launches on a slab), and
  * TMA-stores the partials of the other owners into `stage` (this GPU's memory,
  * [M, N] bf16, block s at rows [s*M/P, (s+1)*M/P)).  An internal stream waits
  * (cuStreamWaitValue32) until each chunk is stored, copies it into slot `rank`

@@ -2501,15 +2501,14 @@ int launch_gemm_rs(const agg_rs_args* a, cudaStream_t stream) {
     // parity on this GPU only.  Each owner's block runs as chunks of gm m-tiles
     // (all n-tiles of a chunk before the next), counted per (owner, chunk): 8
     // slices per tile per launch, so a chunk's copy can start as soon as it is
-    // stored.  Small chunks start the copies early, but every chunk streams all
-    // of W through L2 once: two m-tiles (8 MiB per chunk at N = 8192) while W
-    // fits in L2 with room to spare (<= 64 MiB: the 70B down projection at
-    // P = 8, 59 MB), else the usual group of 12 m-tiles (at P = 2 its W is
-    // 235 MB, and 2-m-tile chunks cost 65 us per launch in DRAM re-reads).
+    // stored.  Default: groups of 12 m-tiles, i.e. whole blocks at P = 8 on the
+    // 70B down projection.  Smaller chunks (AGG_RS_CE_GROUP=2) start the copies
+    // earlier but measured slower there: 1.03 ms with one copy stream and
+    // 0.87 ms with two, against 0.83-0.87 ms with whole 32 MiB blocks; at P = 2
+    // they also stream all of W (235 MB) through L2 once per chunk.
     // At most 128 chunks per owner fit the counter area (flag area + 4 KiB).
     const int L = m_local / 256;
-    const bool w_in_l2 = static_cast<size_t>(a->N) * a->K * 2 <= (size_t(64) << 20);
-    int gm = std::max(1, std::min(L, env_int("AGG_RS_CE_GROUP", w_in_l2 ? 2 : 12)));
+    int gm = std::max(1, std::min(L, env_int("AGG_RS_CE_GROUP", 12)));
     gm = std::max(gm, (L + 127) / 128);
     p.group_m = gm;
     p.rs_ce = 1;
